@@ -1,0 +1,129 @@
+/*
+ * nemo.h -- C ABI of the B200 Nemotron-3-Embed-1B encoder library
+ * (libnemo_b200.so). This is the boundary a host binding (the N-API addon for
+ * the reference's TypeScript engine, or ctypes) calls; no CUDA or torch types
+ * appear in the signatures.
+ *
+ * Threading: a model is immutable after load and may be shared by many plans;
+ * distinct plans may run concurrently from different threads; one plan must
+ * not be run from two threads at once (the reference's engine never does).
+ * Errors: every int-returning call returns NEMO_OK (0) or a negative
+ * nemo_status; nemo_last_error() then describes the failure (thread-local).
+ */
+#ifndef NEMO_H
+#define NEMO_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEMO_HIDDEN 2048       /* embedding width, src/webgpu/model.ts:19 */
+#define NEMO_MAX_BATCH 16      /* src/webgpu/embedding-engine.ts:37 */
+#define NEMO_MAX_SEQUENCE 32768
+#define NEMO_NUM_STAGES 11
+
+typedef enum {
+  NEMO_OK = 0,
+  NEMO_ERR_ARGS = -1,    /* bad argument (shape, length, id range, null pointer) */
+  NEMO_ERR_FORMAT = -2,  /* malformed or unsupported .wgpack */
+  NEMO_ERR_CUDA = -3,    /* CUDA runtime / driver failure */
+  NEMO_ERR_NCCL = -4,    /* collective failure */
+  NEMO_ERR_TIMEOUT = -5, /* a bounded device-side wait gave up */
+  NEMO_ERR_STATE = -6    /* object used in a state that does not allow the call */
+} nemo_status;
+
+typedef struct nemo_model nemo_model;
+typedef struct nemo_plan nemo_plan;
+
+typedef struct {
+  int n_layers;           /* 16 for Nemotron-3-Embed-1B */
+  int vocab;              /* token_embd rows */
+  int n_devices;          /* devices holding a replica */
+  int compact_matrices;   /* projections stored q4_0-tile32-compact */
+  int kquant_matrices;    /* projection parts stored as raw Q4_K / Q6_K / Q4_0 */
+  uint64_t packed_weight_bytes;  /* quantised projection bytes (one replica) */
+  uint64_t device_bytes;         /* device memory held per replica */
+} nemo_model_info;
+
+/* Loads a .wgpack image and uploads one replica per listed CUDA device.
+ * Replaces `new NemotronWebGPUModel(device, parsePrepackedModel(buffer))`
+ * (src/webgpu/model.ts:253-305; src/prepacked/format.ts:146-169). Projections
+ * may be q4_0-tile32-compact fused tensors (attn_qkv, attn_output,
+ * ffn_gate_up, ffn_down) or raw GGML Q4_K / Q6_K / Q4_0 parts (attn_q/k/v,
+ * attn_output, ffn_gate/up/down); they are decoded once to their effective
+ * f16 values on each device. devices == NULL or ndev == 0 selects device 0. */
+int nemo_model_load(const void* wgpack, size_t bytes, const int* devices, int ndev, nemo_model** out);
+
+/* Frees every replica. Plans of the model must be destroyed first. */
+void nemo_model_destroy(nemo_model* model);
+
+int nemo_model_info_get(const nemo_model* model, nemo_model_info* info);
+
+/* Builds an execution plan for micro-batches of up to `batch` requests of up
+ * to `sequence` tokens (buffers, RoPE table, one CUDA graph per device).
+ * Replaces NemotronWebGPUModel.createPlan (src/webgpu/model.ts:328,73-139) and
+ * EmbeddingRuntime.createPlan (src/webgpu/embedding-engine.ts:11-14).
+ * batch in [1, 16], sequence in [1, NEMO_MAX_SEQUENCE]. */
+int nemo_plan_create(nemo_model* model, uint32_t batch, uint32_t sequence, nemo_plan** out);
+
+/* Runs one micro-batch and blocks until the embeddings are in `out`.
+ * Replaces NemotronExecutionPlan.run (src/webgpu/model.ts:146-176) /
+ * EmbeddingPlan.run (src/webgpu/embedding-engine.ts:7-9).
+ * ids: n_ids == batch * sequence token ids, row b padded after lengths[b];
+ * lengths: n_lengths == batch values in [1, sequence] (BOS included);
+ * out: batch * NEMO_HIDDEN floats, L2-normalised, caller-owned.
+ * Errors: NEMO_ERR_ARGS with "token buffer does not match execution plan"
+ * (model.ts:147) for a wrong n_ids; ids >= vocab and lengths outside
+ * [1, sequence] are rejected as well. Requests are spread over the model's
+ * devices when it has more than one. */
+int nemo_plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths,
+                  size_t n_lengths, float* out);
+
+/* Same forward on inputs already resident on the plan's (first) device:
+ * d_ids [batch*sequence] u32, d_lengths [batch] u32, d_out [batch*2048] f32,
+ * all device pointers. Enqueued asynchronously on the plan's stream (see
+ * nemo_plan_stream); the caller synchronises with nemo_plan_synchronize.
+ * Inputs are not validated (lengths are clamped to [1, sequence], ids to the
+ * vocabulary); single-device plans only. */
+int nemo_plan_run_device(nemo_plan* plan, const uint32_t* d_ids, const uint32_t* d_lengths,
+                         float* d_out);
+
+/* cudaStream_t of the plan's first device, as void*. */
+void* nemo_plan_stream(nemo_plan* plan);
+
+/* Waits for the plan's streams; returns NEMO_ERR_TIMEOUT if a kernel reported
+ * a bounded wait giving up. */
+int nemo_plan_synchronize(nemo_plan* plan);
+
+/* Per-stage device time of one forward, summed over layers like
+ * NemotronExecutionPlan.profile (src/webgpu/model.ts:178-224). stage_ms has
+ * NEMO_NUM_STAGES entries in the order of nemo_stage_name(). */
+int nemo_plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths,
+                      size_t n_lengths, float* stage_ms);
+const char* nemo_stage_name(int stage);
+
+/* Parity hook: runs the forward eagerly and copies, after each layer l, the
+ * residual stream and the normalised state (f16 bit patterns) of the valid
+ * tokens, packed request-major, to x_dump + l*batch*sequence*2048 and
+ * norm_dump + ... (either may be NULL); tokens_per_layer[l] receives the row
+ * count. Single-device plans only. */
+int nemo_plan_run_debug(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths,
+                        size_t n_lengths, float* out, uint16_t* x_dump, uint16_t* norm_dump,
+                        int* tokens_per_layer);
+
+/* Frees the plan's buffers, graphs and streams. */
+void nemo_plan_destroy(nemo_plan* plan);
+
+/* contextualMergedLength (src/webgpu/model.ts:30-32). */
+uint32_t nemo_merged_length(uint32_t sequence);
+
+/* Description of the last failure on this thread ("" if none). */
+const char* nemo_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEMO_H */

@@ -1,0 +1,220 @@
+// Shared constants, error plumbing and sm_100a PTX wrappers (mbarrier, TMA,
+// tcgen05) for the Nemotron-3-Embed-1B B200 encoder library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace nemo {
+
+// Architecture constants (src/webgpu/model.ts:19-28, heads at model.ts:127-128).
+constexpr int kHidden = 2048;
+constexpr int kInter = 6144;
+constexpr int kQWidth = 3072;
+constexpr int kKVWidth = 1024;
+constexpr int kQKVWidth = kQWidth + 2 * kKVWidth;  // 5120
+constexpr int kMaxLayers = 16;
+constexpr int kMergeAfterLayer = 4;
+constexpr float kEpsilon = 1e-5f;
+constexpr double kRopeTheta = 1000000.0;
+constexpr int kQHeads = 24;
+constexpr int kKVHeads = 8;
+constexpr int kHeadDim = 128;
+constexpr int kMaxBatch = 16;  // embedding-engine.ts:37
+constexpr int kGemmTileM = 128;
+
+// Status codes of the C ABI (include/nemo.h).
+enum Status {
+  kOk = 0,
+  kErrArgs = -1,
+  kErrFormat = -2,
+  kErrCuda = -3,
+  kErrNccl = -4,
+  kErrTimeout = -5,
+  kErrState = -6,
+};
+
+// Thread-local last-error message, returned by nemo_last_error().
+void set_error(const std::string& msg);
+const char* last_error();
+
+// Error bits a kernel writes to the per-device error word when a bounded wait
+// gives up (so the host can report a timeout instead of hanging).
+constexpr uint32_t kDevErrMbarTimeout = 1u;
+constexpr uint32_t kDevErrBadIndex = 2u;
+
+}  // namespace nemo
+
+#define NEMO_CUDA_TRY(expr)                                                             \
+  do {                                                                                  \
+    cudaError_t _e = (expr);                                                            \
+    if (_e != cudaSuccess) {                                                            \
+      ::nemo::set_error(std::string("CUDA error: ") + cudaGetErrorString(_e) + " at " + \
+                        __FILE__ + ":" + std::to_string(__LINE__) + " (" #expr ")");    \
+      return ::nemo::kErrCuda;                                                          \
+    }                                                                                   \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Device helpers.
+
+namespace nemo {
+namespace dev {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(addr), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(addr), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait on an mbarrier phase. Gives up after `limit_ns` of wall time
+// (read from %globaltimer every 256 polls), records kDevErrMbarTimeout in
+// *err and returns false; the caller then unwinds instead of hanging.
+__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, uint32_t* err,
+                                          uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer() - start > limit_ns) {
+      if (err) atomicOr(err, kDevErrMbarTimeout);
+      return false;
+    }
+  }
+}
+
+// 2-D tiled TMA load (no multicast) into shared memory, completing on `mbar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(mbar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// --- tcgen05 ---------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Arrives on `mbar` once every previously issued tcgen05.mma of this thread
+// has completed.
+__device__ __forceinline__ void tc_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   mbar)
+               : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 inputs, f32 accumulate.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives the
+// 32 columns of TMEM lane (warp quarter * 32 + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored in the
+// canonical 128-byte-swizzle layout: rows of 64 f16 (128 B), 8-row core groups
+// 1024 B apart (stride byte offset), descriptor version 1 (bit 46), layout
+// type SWIZZLE_128B (2) in bits 61-63. The start address advances by 32 B per
+// K=16 step inside the swizzle atom.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                        // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset
+  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: f16 A/B, f32 D, both K-major, M x N.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n) {
+  return (1u << 4)                         // D format f32
+         | (0u << 7) | (0u << 10)          // A, B f16
+         | ((uint32_t)(n >> 3) << 17)      // N >> 3
+         | ((uint32_t)(m >> 4) << 24);     // M >> 4
+}
+
+__device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
+
+}  // namespace dev
+}  // namespace nemo

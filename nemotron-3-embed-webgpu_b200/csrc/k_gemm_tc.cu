@@ -1,0 +1,213 @@
+// Projection GEMM on the 5th-generation tensor cores (tcgen05) for the
+// batched regime: Y[M x N] = X[M x K] . W[N x K]^T with f16 operands and f32
+// accumulation in tensor memory. It replaces the reference's quantised matmul
+// pipelines (src/webgpu/quant-matmul.ts:438-563) for the projections of
+// src/webgpu/model.ts:126-134; the weights are the effective f16 values of the
+// quantised blocks, decoded once at load.
+//
+// One CTA computes a 128 x BN tile. Warp roles (192 threads):
+//   warp 0      TMA producer: 64-wide K slabs of A (128 x 64) and B (BN x 64)
+//               into a STAGES-deep ring, 128-byte swizzled, mbarrier complete_tx
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128,
+//               N=BN, K=16 per instruction), tcgen05.commit frees each stage
+//   warps 2..5  epilogue: tcgen05.ld 32x32b (one row per thread), f16 store
+// Every mbarrier wait is bounded (2 s); a timeout sets the device error word,
+// drains what this CTA has in flight and frees its TMEM before returning.
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+
+namespace nemo {
+namespace {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, __half* y,
+                   int ldy, const int* __restrict__ d_rows, int k, uint32_t* err) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const int M = *d_rows;
+  const int m0 = blockIdx.y * C::BM;
+  if (m0 >= M) return;  // uniform over the CTA
+  const int n0 = blockIdx.x * BN;
+  // 1024-byte alignment of the shared-window address (the 128-byte swizzle
+  // pattern repeats every 1024 bytes and the descriptors assume base offset 0).
+  const uint32_t raw_s = dev::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  const uint32_t full0 = dev::smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * C::STAGES;
+  const uint32_t accum = empty0 + 8 * C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 1);
+  const uint32_t sbase = dev::smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = k / C::BK;
+
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&map_a);
+    dev::prefetch_tmap(&map_b);
+    for (int s = 0; s < C::STAGES; ++s) {
+      dev::mbar_init(full0 + 8 * s, 1);
+      dev::mbar_init(empty0 + 8 * s, 1);
+    }
+    dev::mbar_init(accum, 1);
+    dev::fence_mbar_init();
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), C::TMEM_COLS);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % C::STAGES;
+        const uint32_t ph = (kt / C::STAGES) & 1;
+        if (!dev::mbar_wait(empty0 + 8 * s, ph ^ 1, err)) break;
+        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+        dev::mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES);
+        dev::tma_load_2d(sa, &map_a, kt * C::BK, m0, full0 + 8 * s);
+        dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
+        ++issued;
+      }
+      // Drain: every issued copy has landed before shared memory is released.
+      for (int i = issued > C::STAGES ? issued - C::STAGES : 0; i < issued; ++i)
+        dev::mbar_wait(full0 + 8 * (i % C::STAGES), (i / C::STAGES) & 1, err, 100000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = dev::make_idesc_f16(C::BM, BN);
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % C::STAGES;
+        const uint32_t ph = (kt / C::STAGES) & 1;
+        if (!dev::mbar_wait(full0 + 8 * s, ph, err)) break;
+        dev::tc_fence_after();
+        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          const uint64_t ad = dev::make_sw128_desc(sa + kk * 32);
+          const uint64_t bd = dev::make_sw128_desc(sa + C::A_BYTES + kk * 32);
+          dev::tc_mma_f16(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+        }
+        dev::tc_commit(empty0 + 8 * s);
+      }
+      dev::tc_commit(accum);
+      // All MMAs of this CTA have retired before TMEM is released below.
+      dev::mbar_wait(accum, 0, err, 100000000ull);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    if (dev::mbar_wait(accum, 0, err)) {
+      dev::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        dev::tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + c * 32, r);
+        dev::tc_wait_ld();
+        if (row < M) {
+          uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + n0 + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 u;
+            __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              h[j] = __floats2half2_rn(__uint_as_float(r[v * 8 + 2 * j]), __uint_as_float(r[v * 8 + 2 * j + 1]));
+            dst[v] = u;
+          }
+        }
+      }
+    }
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int BN>
+cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
+                      int max_rows, int n, int k, uint32_t* err, cudaStream_t s) {
+  using C = GemmCfg<BN>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  dim3 grid(n / BN, (max_rows + C::BM - 1) / C::BM);
+  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, err);
+  return cudaGetLastError();
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
+                           int max_rows, int n, int k, int bn, uint32_t* err, cudaStream_t s) {
+  if (k % 64 != 0 || n % bn != 0) return cudaErrorInvalidValue;
+  switch (bn) {
+    case 64: return launch_bn<64>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
+    case 128: return launch_bn<128>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
+    case 256: return launch_bn<256>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                  uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return kErrCuda;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+    return kErrCuda;
+  }
+  return kOk;
+}
+
+}  // namespace nemo

@@ -1,0 +1,81 @@
+// Launch wrappers for every device kernel of the encoder forward pass. Token
+// rows are packed: the valid tokens of request 0, then request 1, ... (padding
+// rows of the reference's [batch x sequence] layout are never computed).
+#pragma once
+
+#include "common.cuh"
+
+namespace nemo {
+
+// Per-run token bookkeeping, built on the device from the request lengths.
+struct Meta {
+  int batch;
+  int seq;         // plan input sequence
+  int merged_seq;  // contextualMergedLength(seq)
+  int t0;          // valid tokens, layers 0..3
+  int t1;          // valid tokens after the layer-4 merge
+  int src_len[kMaxBatch];
+  int tgt_len[kMaxBatch];
+  int src_off[kMaxBatch + 1];
+  int tgt_off[kMaxBatch + 1];
+};
+
+// Weight segment formats accepted by the decoders.
+enum SegFormat { kSegQ4K = 0, kSegQ6K = 1, kSegQ40 = 2, kSegQ40Tile32 = 3 };
+
+// Decodes `rows` rows of a [rows x k] quantised matrix to f16 (the effective
+// weights f16(decode)) and, if out32 != nullptr, to exact f32 values.
+cudaError_t launch_decode(int fmt, const uint8_t* src, int rows, int k, __half* out16, float* out32,
+                          cudaStream_t s);
+
+// model.ts:226-233 on the device: lengths -> Meta. `batch` is the capacity;
+// when run_batch is non-null the run uses min(*run_batch, batch) requests.
+cudaError_t launch_meta(const uint32_t* lengths, int batch, int seq, const uint32_t* run_batch, Meta* meta,
+                        cudaStream_t s);
+
+// ops.ts:680-725. ids: [batch x seq] padded rows; output packed rows.
+cudaError_t launch_embedding(const uint32_t* ids, const uint8_t* table, int vocab, const Meta* meta,
+                             int max_tokens, __half* x, cudaStream_t s);
+
+// ops.ts:21-72. rows = *d_rows (device int). residual may be null.
+cudaError_t launch_residual_rmsnorm(__half* x, const __half* residual, const float* w, __half* norm,
+                                    const int* d_rows, int max_rows, cudaStream_t s);
+
+// ops.ts:168-194. merged selects the post-merge offsets for positions.
+cudaError_t launch_rope(const __half* qkv, const float* table, const Meta* meta, bool merged,
+                        int max_tokens, __half* q, __half* k, cudaStream_t s);
+
+// ops.ts:213-362. q [T x 24 x 128], k [T x 8 x 128], v read from qkv at column
+// 4096 (row stride 5120); out [T x 3072].
+cudaError_t launch_attention(const __half* q, const __half* k, const __half* qkv, const Meta* meta,
+                             bool merged, int batch, int max_len, __half* out, cudaStream_t s);
+
+// ops.ts:74-89 over [rows x 12288] -> [rows x 6144].
+cudaError_t launch_swiglu(const __half* gate_up, const int* d_rows, int max_rows, __half* out,
+                          cudaStream_t s);
+
+// ops.ts:629-661, applied to x and normalized in one launch.
+cudaError_t launch_merge(const __half* x, const __half* norm, const Meta* meta, int max_out,
+                         __half* xm, __half* nm, cudaStream_t s);
+
+// ops.ts:596-616.
+cudaError_t launch_mean_pool(const __half* norm, const Meta* meta, int batch, float* out,
+                             cudaStream_t s);
+
+// Plain CUDA-core f16 GEMM, f32 accumulate: Y[M x N] = X[M x K] . W[N x K]^T,
+// M = *d_rows. A validation kernel for the tensor-core GEMM.
+cudaError_t launch_gemm_simt(const __half* x, const __half* w, __half* y, float* y32,
+                             const int* d_rows, int max_rows, int n, int k, cudaStream_t s);
+
+// tcgen05 GEMM: A = activations via tensor map (box 64 x 128, 128B swizzle),
+// B = f16 weights via tensor map (box 64 x bn). Y row-major [M x ldy] f16.
+cudaError_t launch_gemm_tc(const CUtensorMap* map_a, const CUtensorMap* map_b, __half* y, int ldy,
+                           const int* d_rows, int max_rows, int n, int k, int bn, uint32_t* err,
+                           cudaStream_t s);
+
+// Host: encodes a 2-D f16 tensor map over a row-major [outer x inner] array
+// with a (box_inner x box_outer) box and 128-byte swizzle.
+int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                  uint32_t box_inner, uint32_t box_outer);
+
+}  // namespace nemo

@@ -1,0 +1,268 @@
+// Model load: parse the .wgpack, validate every tensor the forward needs,
+// upload one replica per device and decode each projection once to its
+// effective f16 weights (src/webgpu/model.ts:253-320 + the weight decode of
+// every matmul pipeline). The raw quantised bytes stay resident beside the f16
+// copy. Device memory per replica: ~0.53 GB packed + 1.74 GB f16 + 0.22 GB
+// token table, a small share of a B200's 180 GB.
+#include <string.h>
+
+#include "runtime.h"
+
+namespace nemo {
+namespace {
+
+struct PartSpec {
+  const PackTensor* t;
+  int fmt;
+};
+
+const char* kFused[4] = {"attn_qkv", "attn_output", "ffn_gate_up", "ffn_down"};
+const std::vector<std::vector<const char*>> kParts = {
+    {"attn_q", "attn_k", "attn_v"}, {"attn_output"}, {"ffn_gate", "ffn_up"}, {"ffn_down"}};
+
+int fmt_of(const PackTensor& t, std::string* err) {
+  if (t.compact) return kSegQ40Tile32;
+  switch (t.type) {
+    case kQ4_K: return kSegQ4K;
+    case kQ6_K: return kSegQ6K;
+    case kQ4_0: return kSegQ40;
+    default:
+      *err = "unsupported matrix type " + std::to_string(t.type) + " for " + t.name;  // model.ts:318
+      return -1;
+  }
+}
+
+size_t expected_bytes(int fmt, int64_t rows, int64_t k) {
+  switch (fmt) {
+    case kSegQ4K: return (size_t)(rows * (k / 256) * 144);
+    case kSegQ6K: return (size_t)(rows * (k / 256) * 210);
+    case kSegQ40: return (size_t)(rows * (k / 32) * 18);
+    default: return (size_t)(((rows + 31) / 32) * (k / 32) * 32 * 20);
+  }
+}
+
+template <typename T>
+int dev_alloc(DeviceModel& dm, T** p, size_t bytes) {
+  void* v = nullptr;
+  NEMO_CUDA_TRY(cudaMalloc(&v, bytes));
+  dm.allocations.push_back(v);
+  dm.bytes += bytes;
+  *p = reinterpret_cast<T*>(v);
+  return kOk;
+}
+
+// Resolves the segments of projection `which` of layer l: one compact fused
+// tensor, or the per-part raw tensors in output-column order.
+int resolve(const Pack& pack, int l, int which, std::vector<PartSpec>* parts, std::string* err) {
+  const std::string prefix = "blk." + std::to_string(l) + ".";
+  auto it = pack.tensors.find(prefix + kFused[which] + ".weight");
+  if (it != pack.tensors.end() && (it->second.compact || kParts[which].size() == 1)) {
+    int fmt = fmt_of(it->second, err);
+    if (fmt < 0) return kErrFormat;
+    parts->push_back({&it->second, fmt});
+    return kOk;
+  }
+  for (const char* pn : kParts[which]) {
+    auto jt = pack.tensors.find(prefix + pn + ".weight");
+    if (jt == pack.tensors.end()) {
+      *err = "missing tensor " + prefix + (kParts[which].size() > 1 ? kFused[which] : pn) + ".weight";
+      return kErrFormat;
+    }
+    int fmt = fmt_of(jt->second, err);
+    if (fmt < 0) return kErrFormat;
+    parts->push_back({&jt->second, fmt});
+  }
+  return kOk;
+}
+
+int upload_replica(const uint8_t* file, const Pack& pack, int n_layers, int vocab, DeviceModel& dm,
+                   nemo_model* m, bool count) {
+  NEMO_CUDA_TRY(cudaSetDevice(dm.device));
+  const PackTensor& te = pack.tensors.at("token_embd.weight");
+  if (dev_alloc(dm, &dm.embd, te.byte_length)) return kErrCuda;
+  NEMO_CUDA_TRY(cudaMemcpy(dm.embd, file + te.byte_offset, te.byte_length, cudaMemcpyHostToDevice));
+  auto norm = [&](const std::string& name, float** dst) -> int {
+    const PackTensor& t = pack.tensors.at(name);
+    if (dev_alloc(dm, dst, t.byte_length)) return kErrCuda;
+    NEMO_CUDA_TRY(cudaMemcpy(*dst, file + t.byte_offset, t.byte_length, cudaMemcpyHostToDevice));
+    return kOk;
+  };
+  for (int l = 0; l < n_layers; ++l) {
+    if (norm("blk." + std::to_string(l) + ".attn_norm.weight", &dm.attn_norm[l])) return kErrCuda;
+    if (norm("blk." + std::to_string(l) + ".ffn_norm.weight", &dm.ffn_norm[l])) return kErrCuda;
+  }
+  if (norm("output_norm.weight", &dm.output_norm)) return kErrCuda;
+
+  for (int l = 0; l < n_layers; ++l) {
+    for (int which = 0; which < 4; ++which) {
+      std::vector<PartSpec> parts;
+      std::string err;
+      if (resolve(pack, l, which, &parts, &err)) {
+        set_error(err);
+        return kErrFormat;
+      }
+      Projection& pr = dm.proj[l][which];
+      pr.n = kProjN[which];
+      pr.k = kProjK[which];
+      if (dev_alloc(dm, &pr.w16, (size_t)pr.n * pr.k * 2)) return kErrCuda;
+      int row0 = 0;
+      for (const PartSpec& ps : parts) {
+        Segment sg;
+        sg.fmt = ps.fmt;
+        sg.row0 = row0;
+        sg.rows = (int)ps.t->dims[1];
+        sg.bytes = ps.t->byte_length;
+        if (dev_alloc(dm, &sg.raw, sg.bytes)) return kErrCuda;
+        NEMO_CUDA_TRY(cudaMemcpy(sg.raw, file + ps.t->byte_offset, sg.bytes, cudaMemcpyHostToDevice));
+        NEMO_CUDA_TRY(launch_decode(sg.fmt, sg.raw, sg.rows, pr.k, pr.w16 + (size_t)row0 * pr.k, nullptr, 0));
+        if (count) {
+          if (sg.fmt == kSegQ40Tile32) m->compact++;
+          else m->kquant++;
+          m->packed_bytes += sg.bytes;
+        }
+        row0 += sg.rows;
+        pr.segs.push_back(sg);
+      }
+      for (int b = 0; b < kNumBn; ++b)
+        if (int rc = make_tmap_f16(&pr.map[b], pr.w16, (uint64_t)pr.k, (uint64_t)pr.n, 64, kBnChoices[b])) return rc;
+    }
+  }
+  NEMO_CUDA_TRY(cudaDeviceSynchronize());
+  return kOk;
+}
+
+// Validation of everything the forward reads (format.ts checks are done by
+// parse_wgpack; these mirror model.ts:278,309,315,318 for this build).
+int validate(const Pack& pack, int* n_layers, int* vocab) {
+  int layers = 0;
+  while (layers < kMaxLayers && pack.tensors.count("blk." + std::to_string(layers) + ".attn_norm.weight")) ++layers;
+  if (layers < kMergeAfterLayer + 1) {
+    set_error("pack has " + std::to_string(layers) + " layers; expected 16 (at least 5 for reduced test packs)");
+    return kErrFormat;
+  }
+  auto te = pack.tensors.find("token_embd.weight");
+  if (te == pack.tensors.end()) {
+    set_error("missing tensor token_embd.weight");
+    return kErrFormat;
+  }
+  const PackTensor& t = te->second;
+  if (t.type != kQ6_K || t.compact || t.dims.size() != 2 || t.dims[0] != kHidden || t.dims[1] < 1 ||
+      t.byte_length != (uint64_t)t.dims[1] * (kHidden / 256) * 210) {
+    set_error("token_embd.weight must be raw Q6_K [2048 x vocab]");
+    return kErrFormat;
+  }
+  *vocab = (int)t.dims[1];
+  auto check_norm = [&](const std::string& name) -> bool {
+    auto it = pack.tensors.find(name);
+    if (it == pack.tensors.end()) {
+      set_error("missing tensor " + name);
+      return false;
+    }
+    if (it->second.type != kF32 || it->second.compact || it->second.byte_length != kHidden * 4) {
+      set_error(name + " must be raw F32 [2048]");
+      return false;
+    }
+    return true;
+  };
+  for (int l = 0; l < layers; ++l) {
+    if (!check_norm("blk." + std::to_string(l) + ".attn_norm.weight")) return kErrFormat;
+    if (!check_norm("blk." + std::to_string(l) + ".ffn_norm.weight")) return kErrFormat;
+    for (int which = 0; which < 4; ++which) {
+      std::vector<PartSpec> parts;
+      std::string err;
+      if (resolve(pack, l, which, &parts, &err)) {
+        set_error(err);
+        return kErrFormat;
+      }
+      int64_t rows = 0;
+      for (const PartSpec& ps : parts) {
+        const PackTensor& pt = *ps.t;
+        if (pt.dims.size() != 2 || pt.dims[0] != kProjK[which]) {
+          set_error("invalid matrix " + pt.name);  // model.ts:315
+          return kErrFormat;
+        }
+        if ((ps.fmt == kSegQ4K || ps.fmt == kSegQ6K) && pt.dims[0] % 256 != 0) {
+          set_error(pt.name + " K is not divisible by a K-quant block");
+          return kErrFormat;
+        }
+        if (pt.byte_length != expected_bytes(ps.fmt, pt.dims[1], pt.dims[0])) {
+          set_error(pt.name + " has " + std::to_string(pt.byte_length) + " bytes; expected " +
+                    std::to_string(expected_bytes(ps.fmt, pt.dims[1], pt.dims[0])));
+          return kErrFormat;
+        }
+        if (pt.dims[1] % 128 != 0 && parts.size() > 1) {
+          set_error(pt.name + " rows must be a multiple of 128");
+          return kErrFormat;
+        }
+        rows += pt.dims[1];
+      }
+      if (rows != kProjN[which]) {
+        set_error("blk." + std::to_string(l) + "." + kFused[which] + " has " + std::to_string(rows) +
+                  " output rows; expected " + std::to_string(kProjN[which]));
+        return kErrFormat;
+      }
+    }
+  }
+  if (!check_norm("output_norm.weight")) return kErrFormat;
+  *n_layers = layers;
+  return kOk;
+}
+
+void free_replica(DeviceModel& dm) {
+  cudaSetDevice(dm.device);
+  for (void* p : dm.allocations) cudaFree(p);
+  dm.allocations.clear();
+}
+
+}  // namespace
+
+int model_load(const void* data, size_t bytes, const int* devices, int ndev, nemo_model** out) {
+  if (!data || !out) {
+    set_error("nemo_model_load: null argument");
+    return kErrArgs;
+  }
+  *out = nullptr;
+  Pack pack;
+  std::string err;
+  if (!parse_wgpack(reinterpret_cast<const uint8_t*>(data), bytes, &pack, &err)) {
+    set_error(err);
+    return kErrFormat;
+  }
+  int n_layers = 0, vocab = 0;
+  if (int rc = validate(pack, &n_layers, &vocab)) return rc;
+  int count = 0;
+  NEMO_CUDA_TRY(cudaGetDeviceCount(&count));
+  std::vector<int> devs;
+  if (!devices || ndev <= 0) devs.push_back(0);
+  else devs.assign(devices, devices + ndev);
+  for (int d : devs)
+    if (d < 0 || d >= count) {
+      set_error("device " + std::to_string(d) + " is not present (" + std::to_string(count) + " devices)");
+      return kErrArgs;
+    }
+  auto* m = new nemo_model();
+  m->n_layers = n_layers;
+  m->vocab = vocab;
+  for (size_t i = 0; i < devs.size(); ++i) {
+    auto dm = std::make_unique<DeviceModel>();
+    dm->device = devs[i];
+    dm->vocab = vocab;
+    int rc = upload_replica(reinterpret_cast<const uint8_t*>(data), pack, n_layers, vocab, *dm, m, i == 0);
+    m->devs.push_back(std::move(dm));
+    if (rc) {
+      for (auto& d : m->devs) free_replica(*d);
+      delete m;
+      return rc;
+    }
+  }
+  *out = m;
+  return kOk;
+}
+
+void model_destroy(nemo_model* m) {
+  if (!m) return;
+  for (auto& d : m->devs) free_replica(*d);
+  delete m;
+}
+
+}  // namespace nemo

@@ -1,0 +1,495 @@
+// Execution plans: the B200 counterpart of NemotronExecutionPlan
+// (src/webgpu/model.ts:58-234). A plan owns, per device, buffers sized for its
+// worst case (capacity batch x sequence tokens), the RoPE table, and two CUDA
+// graphs captured once at creation:
+//   graph_host    H2D ids/lengths from pinned staging -> forward -> D2H output
+//   graph_device  forward only (inputs already resident)
+// Kernels read the run's token counts from device metadata, so one graph
+// serves every run of the plan whatever the request lengths (only valid
+// tokens are computed; padding rows are skipped, not masked).
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <numeric>
+
+#include "runtime.h"
+
+namespace nemo {
+
+int model_load(const void* data, size_t bytes, const int* devices, int ndev, nemo_model** out);
+void model_destroy(nemo_model* m);
+
+const char* kStageNames[11] = {"embedding_norm", "token_merge",  "qkv",         "rope_attention",
+                               "attention_output", "post_attention_norm", "ffn_up_gate", "swiglu",
+                               "ffn_down",         "post_ffn_norm",       "pool"};
+
+struct Profile {
+  std::vector<cudaEvent_t> events;
+  std::vector<int> ids;
+};
+
+struct Dump {
+  uint16_t* x = nullptr;
+  uint16_t* norm = nullptr;
+  int* tokens = nullptr;
+  size_t stride = 0;
+};
+
+namespace {
+
+int pick_bn(int rows, int n) {
+  const int mt = (rows + kGemmTileM - 1) / kGemmTileM;
+  if ((long long)mt * (n / 256) >= 148) return 2;
+  if ((long long)mt * (n / 128) >= 148) return 1;
+  return 0;
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+template <typename T>
+int plan_alloc(DevicePlan& p, T** ptr, size_t bytes) {
+  void* v = nullptr;
+  NEMO_CUDA_TRY(cudaMalloc(&v, bytes));
+  NEMO_CUDA_TRY(cudaMemset(v, 0, bytes));
+  p.allocations.push_back(v);
+  *ptr = reinterpret_cast<T*>(v);
+  return kOk;
+}
+
+void free_device_plan(DevicePlan& p) {
+  cudaSetDevice(p.device);
+  if (p.graph_host) cudaGraphExecDestroy(p.graph_host);
+  if (p.graph_device) cudaGraphExecDestroy(p.graph_device);
+  for (void* v : p.allocations) cudaFree(v);
+  if (p.h_ids) cudaFreeHost(p.h_ids);
+  if (p.h_lengths) cudaFreeHost(p.h_lengths);
+  if (p.h_out) cudaFreeHost(p.h_out);
+  if (p.h_err) cudaFreeHost(p.h_err);
+  if (p.stream) cudaStreamDestroy(p.stream);
+  p = DevicePlan();
+}
+
+}  // namespace
+
+#define NEMO_LAUNCH(expr)                                                                              \
+  do {                                                                                                 \
+    cudaError_t _e = (expr);                                                                           \
+    if (_e != cudaSuccess) {                                                                           \
+      set_error(std::string("kernel launch failed: ") + cudaGetErrorString(_e) + " (" #expr ")");      \
+      return kErrCuda;                                                                                 \
+    }                                                                                                  \
+  } while (0)
+
+// Enqueues one forward pass (model.ts:152-168) on stream s.
+int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, Dump* dump) {
+  DeviceModel& dm = *p.dm;
+  auto stage = [&](int id) {
+    if (!prof) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, s);
+    prof->events.push_back(e);
+    prof->ids.push_back(id);
+  };
+  const int* t0 = &p.meta->t0;
+  const int* t1 = &p.meta->t1;
+  NEMO_LAUNCH(launch_meta(p.lengths, p.cap_batch, p.seq, p.lengths + p.cap_batch, p.meta, s));
+  Meta host_meta;
+  if (dump) {
+    NEMO_CUDA_TRY(cudaMemcpyAsync(&host_meta, p.meta, sizeof(Meta), cudaMemcpyDeviceToHost, s));
+    NEMO_CUDA_TRY(cudaStreamSynchronize(s));
+  }
+  stage(0);
+  NEMO_LAUNCH(launch_embedding(p.ids, dm.embd, dm.vocab, p.meta, p.tmax0, p.x, s));
+  NEMO_LAUNCH(launch_residual_rmsnorm(p.x, nullptr, dm.attn_norm[0], p.norm, t0, p.tmax0, s));
+  for (int l = 0; l < n_layers; ++l) {
+    const bool merged = l >= kMergeAfterLayer;
+    if (l == kMergeAfterLayer) {
+      stage(1);
+      NEMO_LAUNCH(launch_merge(p.x, p.norm, p.meta, p.tmax1, p.xm, p.nm, s));
+    }
+    __half* X = merged ? p.xm : p.x;
+    __half* N = merged ? p.nm : p.norm;
+    const CUtensorMap* mapN = merged ? &p.map_norm1 : &p.map_norm0;
+    const int* rows = merged ? t1 : t0;
+    const int maxr = merged ? p.tmax1 : p.tmax0;
+    Projection* pr = dm.proj[l];
+    stage(2);
+    NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth, kHidden,
+                               kBnChoices[p.bn[l][0]], p.err, s));
+    stage(3);
+    NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
+    NEMO_LAUNCH(launch_attention(p.q, p.k, p.qkv, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, s));
+    stage(4);
+    NEMO_LAUNCH(launch_gemm_tc(&p.map_attn, &pr[kProjO].map[p.bn[l][1]], p.delta, kHidden, rows, maxr, kHidden, kQWidth,
+                               kBnChoices[p.bn[l][1]], p.err, s));
+    stage(5);
+    NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, dm.ffn_norm[l], N, rows, maxr, s));
+    stage(6);
+    NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjGateUp].map[p.bn[l][2]], p.gu, 2 * kInter, rows, maxr, 2 * kInter,
+                               kHidden, kBnChoices[p.bn[l][2]], p.err, s));
+    stage(7);
+    NEMO_LAUNCH(launch_swiglu(p.gu, rows, maxr, p.ffn, s));
+    stage(8);
+    NEMO_LAUNCH(launch_gemm_tc(&p.map_ffn, &pr[kProjDown].map[p.bn[l][3]], p.delta, kHidden, rows, maxr, kHidden,
+                               kInter, kBnChoices[p.bn[l][3]], p.err, s));
+    stage(9);
+    const float* next = l + 1 < n_layers ? dm.attn_norm[l + 1] : dm.output_norm;
+    NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, next, N, rows, maxr, s));
+    if (dump) {
+      const int T = merged ? host_meta.t1 : host_meta.t0;
+      if (dump->tokens) dump->tokens[l] = T;
+      if (dump->x)
+        NEMO_CUDA_TRY(cudaMemcpyAsync(dump->x + (size_t)l * dump->stride, X, (size_t)T * kHidden * 2,
+                                      cudaMemcpyDeviceToHost, s));
+      if (dump->norm)
+        NEMO_CUDA_TRY(cudaMemcpyAsync(dump->norm + (size_t)l * dump->stride, N, (size_t)T * kHidden * 2,
+                                      cudaMemcpyDeviceToHost, s));
+      NEMO_CUDA_TRY(cudaStreamSynchronize(s));
+    }
+  }
+  stage(10);
+  NEMO_LAUNCH(launch_mean_pool(p.nm, p.meta, p.cap_batch, p.out, s));
+  stage(-1);
+  return kOk;
+}
+
+namespace {
+
+int capture(DevicePlan& p, int n_layers, bool host_io, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  NEMO_CUDA_TRY(cudaStreamBeginCapture(p.stream, cudaStreamCaptureModeThreadLocal));
+  int rc = kOk;
+  auto body = [&]() -> int {
+    NEMO_CUDA_TRY(cudaMemsetAsync(p.err, 0, 4, p.stream));
+    if (host_io) {
+      NEMO_CUDA_TRY(cudaMemcpyAsync(p.ids, p.h_ids, (size_t)p.cap_batch * p.seq * 4, cudaMemcpyHostToDevice, p.stream));
+      NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths, p.h_lengths, (size_t)(p.cap_batch + 1) * 4, cudaMemcpyHostToDevice,
+                                    p.stream));
+    }
+    if (int r = enqueue_forward(p, n_layers, p.stream, nullptr, nullptr)) return r;
+    if (host_io) {
+      NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_out, p.out, (size_t)p.cap_batch * kHidden * 4, cudaMemcpyDeviceToHost,
+                                    p.stream));
+    }
+    NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_err, p.err, 4, cudaMemcpyDeviceToHost, p.stream));
+    return kOk;
+  };
+  rc = body();
+  cudaError_t e = cudaStreamEndCapture(p.stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error(std::string("graph capture failed: ") + cudaGetErrorString(e));
+    return kErrCuda;
+  }
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error(std::string("graph instantiate failed: ") + cudaGetErrorString(e));
+    return kErrCuda;
+  }
+  return kOk;
+}
+
+int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, DevicePlan& p) {
+  p.device = dm->device;
+  p.dm = dm;
+  p.cap_batch = cap_batch;
+  p.seq = seq;
+  p.mseq = (int)std::max(1.0, ceil(seq * 0.64));
+  p.tmax0 = cap_batch * seq;
+  p.tmax1 = cap_batch * p.mseq;
+  p.rows0 = round_up(p.tmax0, kGemmTileM);
+  p.rows1 = round_up(p.tmax1, kGemmTileM);
+  NEMO_CUDA_TRY(cudaSetDevice(p.device));
+  NEMO_CUDA_TRY(cudaStreamCreateWithFlags(&p.stream, cudaStreamNonBlocking));
+  const size_t r0 = p.rows0, r1 = p.rows1;
+  if (plan_alloc(p, &p.ids, (size_t)p.tmax0 * 4) || plan_alloc(p, &p.lengths, (size_t)(cap_batch + 1) * 4) ||
+      plan_alloc(p, &p.meta, sizeof(Meta)) || plan_alloc(p, &p.err, 256) ||
+      plan_alloc(p, &p.rope, (size_t)seq * 128 * 4) || plan_alloc(p, &p.x, r0 * kHidden * 2) ||
+      plan_alloc(p, &p.norm, r0 * kHidden * 2) || plan_alloc(p, &p.xm, r1 * kHidden * 2) ||
+      plan_alloc(p, &p.nm, r1 * kHidden * 2) || plan_alloc(p, &p.qkv, r0 * kQKVWidth * 2) ||
+      plan_alloc(p, &p.q, r0 * kQWidth * 2) || plan_alloc(p, &p.k, r0 * kKVWidth * 2) ||
+      plan_alloc(p, &p.attn, r0 * kQWidth * 2) || plan_alloc(p, &p.delta, r0 * kHidden * 2) ||
+      plan_alloc(p, &p.gu, r0 * 2 * kInter * 2) || plan_alloc(p, &p.ffn, r0 * kInter * 2) ||
+      plan_alloc(p, &p.out, (size_t)cap_batch * kHidden * 4))
+    return kErrCuda;
+  NEMO_CUDA_TRY(cudaMallocHost(&p.h_ids, (size_t)p.tmax0 * 4));
+  NEMO_CUDA_TRY(cudaMallocHost(&p.h_lengths, (size_t)(cap_batch + 1) * 4));
+  NEMO_CUDA_TRY(cudaMallocHost(&p.h_out, (size_t)cap_batch * kHidden * 4));
+  NEMO_CUDA_TRY(cudaMallocHost(&p.h_err, 4));
+  for (int i = 0; i < p.tmax0; ++i) p.h_ids[i] = 0;
+  for (int b = 0; b < cap_batch; ++b) p.h_lengths[b] = 1;
+  p.h_lengths[cap_batch] = cap_batch;
+  *p.h_err = 0;
+  // model.ts:95-107 (f64 math, stored f32).
+  std::vector<float> rope((size_t)seq * 128);
+  rope_table_host(seq, rope.data());
+  NEMO_CUDA_TRY(cudaMemcpy(p.rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
+  if (make_tmap_f16(&p.map_norm0, p.norm, kHidden, r0, 64, kGemmTileM) ||
+      make_tmap_f16(&p.map_norm1, p.nm, kHidden, r1, 64, kGemmTileM) ||
+      make_tmap_f16(&p.map_attn, p.attn, kQWidth, r0, 64, kGemmTileM) ||
+      make_tmap_f16(&p.map_ffn, p.ffn, kInter, r0, 64, kGemmTileM))
+    return kErrCuda;
+  for (int l = 0; l < m->n_layers; ++l) {
+    const int rows = l >= kMergeAfterLayer ? p.rows1 : p.rows0;
+    for (int w = 0; w < 4; ++w) p.bn[l][w] = pick_bn(rows, kProjN[w]);
+  }
+  // The lengths buffer must hold a valid run before the first launch.
+  NEMO_CUDA_TRY(cudaMemcpy(p.lengths, p.h_lengths, (size_t)(cap_batch + 1) * 4, cudaMemcpyHostToDevice));
+  if (int rc = capture(p, m->n_layers, true, &p.graph_host)) return rc;
+  if (int rc = capture(p, m->n_layers, false, &p.graph_device)) return rc;
+  return kOk;
+}
+
+}  // namespace
+
+void rope_table_host(int sequence, float* table) {
+  const double frequency_scale = 1.0 / 16.0;
+  auto correction = [](double beta) {
+    return 128.0 * log(16384.0 / (beta * 2.0 * M_PI)) / (2.0 * log(kRopeTheta));
+  };
+  const double low = floor(correction(32.0));
+  const double high = ceil(correction(1.0));
+  for (int pos = 0; pos < sequence; ++pos)
+    for (int d = 0; d < 64; ++d) {
+      double t = (d - low) / fmax(0.001, high - low);
+      t = fmin(1.0, fmax(0.0, t));
+      const double ramp = 1.0 - t;
+      const double frequency = frequency_scale * (1.0 - ramp) + ramp;
+      const double angle = pos * pow(kRopeTheta, -d / 64.0) * frequency;
+      table[((size_t)pos * 64 + d) * 2] = (float)cos(angle);
+      table[((size_t)pos * 64 + d) * 2 + 1] = (float)sin(angle);
+    }
+}
+
+int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out) {
+  if (!m || !out) {
+    set_error("nemo_plan_create: null argument");
+    return kErrArgs;
+  }
+  *out = nullptr;
+  if (batch < 1 || batch > (uint32_t)kMaxBatch) {
+    set_error("batch must be between 1 and 16");
+    return kErrArgs;
+  }
+  if (seq < 1 || seq > 32768u) {
+    set_error("sequence must be between 1 and 32768");
+    return kErrArgs;
+  }
+  auto* plan = new nemo_plan();
+  plan->model = m;
+  plan->batch = (int)batch;
+  plan->seq = (int)seq;
+  for (auto& dm : m->devs) {
+    auto dp = std::make_unique<DevicePlan>();
+    int rc = create_device_plan(m, dm.get(), (int)batch, (int)seq, *dp);
+    plan->devs.push_back(std::move(dp));
+    if (rc) {
+      for (auto& d : plan->devs) free_device_plan(*d);
+      delete plan;
+      return rc;
+    }
+  }
+  *out = plan;
+  return kOk;
+}
+
+void plan_destroy(nemo_plan* plan) {
+  if (!plan) return;
+  for (auto& d : plan->devs) {
+    cudaSetDevice(d->device);
+    cudaStreamSynchronize(d->stream);
+    free_device_plan(*d);
+  }
+  delete plan;
+}
+
+namespace {
+
+int validate_inputs(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths) {
+  if (!ids || !lengths) {
+    set_error("null ids or lengths");
+    return kErrArgs;
+  }
+  if (n_ids != (size_t)plan->batch * plan->seq) {
+    set_error("token buffer does not match execution plan");  // model.ts:147
+    return kErrArgs;
+  }
+  if (n_lengths != (size_t)plan->batch) {
+    set_error("lengths buffer does not match execution plan batch");
+    return kErrArgs;
+  }
+  for (int b = 0; b < plan->batch; ++b)
+    if (lengths[b] < 1 || lengths[b] > (uint32_t)plan->seq) {
+      set_error("lengths[" + std::to_string(b) + "] = " + std::to_string(lengths[b]) + " is outside [1, sequence]");
+      return kErrArgs;
+    }
+  const uint32_t vocab = (uint32_t)plan->model->vocab;
+  for (int b = 0; b < plan->batch; ++b)
+    for (uint32_t i = 0; i < lengths[b]; ++i)
+      if (ids[(size_t)b * plan->seq + i] >= vocab) {
+        set_error("token id " + std::to_string(ids[(size_t)b * plan->seq + i]) + " is outside the vocabulary");
+        return kErrArgs;
+      }
+  return kOk;
+}
+
+int check_err(DevicePlan& d) {
+  if (*d.h_err) {
+    set_error("a device-side bounded wait timed out (error word " + std::to_string(*d.h_err) + ")");
+    return kErrTimeout;
+  }
+  return kOk;
+}
+
+}  // namespace
+
+int plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
+             float* out) {
+  if (!plan || !out) {
+    set_error("nemo_plan_run: null argument");
+    return kErrArgs;
+  }
+  if (int rc = validate_inputs(plan, ids, n_ids, lengths, n_lengths)) return rc;
+  const int ndev = (int)plan->devs.size();
+  // Request sharding: longest first onto the device with the fewest tokens.
+  std::vector<std::vector<int>> assign(ndev);
+  if (ndev == 1) {
+    assign[0].resize(plan->batch);
+    std::iota(assign[0].begin(), assign[0].end(), 0);
+  } else {
+    std::vector<int> order(plan->batch);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lengths[a] > lengths[b]; });
+    std::vector<long long> load(ndev, 0);
+    for (int r : order) {
+      const int d = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+      assign[d].push_back(r);
+      load[d] += lengths[r];
+    }
+  }
+  for (int d = 0; d < ndev; ++d) {
+    DevicePlan& p = *plan->devs[d];
+    if (assign[d].empty()) continue;
+    for (size_t j = 0; j < assign[d].size(); ++j) {
+      const int r = assign[d][j];
+      memcpy(p.h_ids + j * p.seq, ids + (size_t)r * plan->seq, (size_t)plan->seq * 4);
+      p.h_lengths[j] = lengths[r];
+    }
+    p.h_lengths[p.cap_batch] = (uint32_t)assign[d].size();
+    NEMO_CUDA_TRY(cudaSetDevice(p.device));
+    NEMO_CUDA_TRY(cudaGraphLaunch(p.graph_host, p.stream));
+  }
+  int rc = kOk;
+  for (int d = 0; d < ndev; ++d) {
+    DevicePlan& p = *plan->devs[d];
+    if (assign[d].empty()) continue;
+    NEMO_CUDA_TRY(cudaSetDevice(p.device));
+    NEMO_CUDA_TRY(cudaStreamSynchronize(p.stream));
+    if (int e = check_err(p)) rc = e;
+    for (size_t j = 0; j < assign[d].size(); ++j)
+      memcpy(out + (size_t)assign[d][j] * kHidden, p.h_out + j * kHidden, kHidden * 4);
+  }
+  return rc;
+}
+
+int plan_run_device(nemo_plan* plan, const uint32_t* d_ids, const uint32_t* d_lengths, float* d_out) {
+  if (!plan || !d_ids || !d_lengths || !d_out) {
+    set_error("nemo_plan_run_device: null argument");
+    return kErrArgs;
+  }
+  if (plan->devs.size() != 1) {
+    set_error("nemo_plan_run_device needs a single-device plan");
+    return kErrState;
+  }
+  DevicePlan& p = *plan->devs[0];
+  NEMO_CUDA_TRY(cudaSetDevice(p.device));
+  p.h_lengths[p.cap_batch] = (uint32_t)p.cap_batch;
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.ids, d_ids, (size_t)p.cap_batch * p.seq * 4, cudaMemcpyDeviceToDevice, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths, d_lengths, (size_t)p.cap_batch * 4, cudaMemcpyDeviceToDevice, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths + p.cap_batch, p.h_lengths + p.cap_batch, 4, cudaMemcpyHostToDevice,
+                                p.stream));
+  NEMO_CUDA_TRY(cudaGraphLaunch(p.graph_device, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(d_out, p.out, (size_t)p.cap_batch * kHidden * 4, cudaMemcpyDeviceToDevice, p.stream));
+  return kOk;
+}
+
+int plan_synchronize(nemo_plan* plan) {
+  if (!plan) return kErrArgs;
+  int rc = kOk;
+  for (auto& d : plan->devs) {
+    NEMO_CUDA_TRY(cudaSetDevice(d->device));
+    NEMO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+    if (int e = check_err(*d)) rc = e;
+  }
+  return rc;
+}
+
+static int stage_host_inputs(nemo_plan* plan, DevicePlan& p, const uint32_t* ids, const uint32_t* lengths) {
+  memcpy(p.h_ids, ids, (size_t)plan->batch * plan->seq * 4);
+  for (int b = 0; b < plan->batch; ++b) p.h_lengths[b] = lengths[b];
+  p.h_lengths[p.cap_batch] = (uint32_t)plan->batch;
+  NEMO_CUDA_TRY(cudaSetDevice(p.device));
+  NEMO_CUDA_TRY(cudaMemsetAsync(p.err, 0, 4, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.ids, p.h_ids, (size_t)p.tmax0 * 4, cudaMemcpyHostToDevice, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths, p.h_lengths, (size_t)(p.cap_batch + 1) * 4, cudaMemcpyHostToDevice,
+                                p.stream));
+  return kOk;
+}
+
+int plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
+                 float* stage_ms) {
+  if (!plan || !stage_ms) {
+    set_error("nemo_plan_profile: null argument");
+    return kErrArgs;
+  }
+  if (int rc = validate_inputs(plan, ids, n_ids, lengths, n_lengths)) return rc;
+  DevicePlan& p = *plan->devs[0];
+  if (int rc = stage_host_inputs(plan, p, ids, lengths)) return rc;
+  Profile prof;
+  int rc = enqueue_forward(p, plan->model->n_layers, p.stream, &prof, nullptr);
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_err, p.err, 4, cudaMemcpyDeviceToHost, p.stream));
+  NEMO_CUDA_TRY(cudaStreamSynchronize(p.stream));
+  for (int i = 0; i < 11; ++i) stage_ms[i] = 0.f;
+  for (size_t i = 0; i + 1 < prof.events.size(); ++i) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, prof.events[i], prof.events[i + 1]);
+    if (prof.ids[i] >= 0) stage_ms[prof.ids[i]] += ms;
+  }
+  for (cudaEvent_t e : prof.events) cudaEventDestroy(e);
+  if (rc) return rc;
+  return check_err(p);
+}
+
+int plan_run_debug(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
+                   float* out, uint16_t* x_dump, uint16_t* norm_dump, int* tokens_per_layer) {
+  if (!plan || !out) {
+    set_error("nemo_plan_run_debug: null argument");
+    return kErrArgs;
+  }
+  if (plan->devs.size() != 1) {
+    set_error("nemo_plan_run_debug needs a single-device plan");
+    return kErrState;
+  }
+  if (int rc = validate_inputs(plan, ids, n_ids, lengths, n_lengths)) return rc;
+  DevicePlan& p = *plan->devs[0];
+  if (int rc = stage_host_inputs(plan, p, ids, lengths)) return rc;
+  Dump dump;
+  dump.x = x_dump;
+  dump.norm = norm_dump;
+  dump.tokens = tokens_per_layer;
+  dump.stride = (size_t)plan->batch * plan->seq * kHidden;
+  if (int rc = enqueue_forward(p, plan->model->n_layers, p.stream, nullptr, &dump)) return rc;
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_out, p.out, (size_t)plan->batch * kHidden * 4, cudaMemcpyDeviceToHost, p.stream));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_err, p.err, 4, cudaMemcpyDeviceToHost, p.stream));
+  NEMO_CUDA_TRY(cudaStreamSynchronize(p.stream));
+  memcpy(out, p.h_out, (size_t)plan->batch * kHidden * 4);
+  return check_err(p);
+}
+
+}  // namespace nemo

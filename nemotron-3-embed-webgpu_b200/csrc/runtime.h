@@ -1,0 +1,102 @@
+// Host-side objects behind the C ABI: per-device model replicas and plans.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "wgpack.h"
+
+struct nemo_model;
+struct nemo_plan;
+
+namespace nemo {
+
+constexpr int kProjQKV = 0, kProjO = 1, kProjGateUp = 2, kProjDown = 3;
+constexpr int kProjN[4] = {kQKVWidth, kHidden, 2 * kInter, kHidden};
+constexpr int kProjK[4] = {kHidden, kQWidth, kHidden, kInter};
+constexpr int kNumBn = 3;
+constexpr int kBnChoices[kNumBn] = {64, 128, 256};
+
+// A row range of a projection stored in one quantised format.
+struct Segment {
+  int fmt = 0;        // SegFormat
+  int row0 = 0;
+  int rows = 0;
+  uint8_t* raw = nullptr;  // device copy of the pack bytes
+  size_t bytes = 0;
+};
+
+struct Projection {
+  int n = 0, k = 0;
+  __half* w16 = nullptr;     // effective f16 weights, [n x k] row-major
+  CUtensorMap map[kNumBn];   // TMA maps over w16, box 64 x bn
+  std::vector<Segment> segs;
+};
+
+struct DeviceModel {
+  int device = 0;
+  uint8_t* embd = nullptr;   // Q6_K token table, vocab x 8 blocks x 210 B
+  int vocab = 0;
+  float* attn_norm[kMaxLayers] = {};
+  float* ffn_norm[kMaxLayers] = {};
+  float* output_norm = nullptr;
+  Projection proj[kMaxLayers][4];
+  std::vector<void*> allocations;
+  size_t bytes = 0;
+};
+
+// One device's share of a plan: buffers sized for the plan's worst case
+// (capacity batch x sequence), pinned staging, and the captured graph.
+struct DevicePlan {
+  int device = 0;
+  DeviceModel* dm = nullptr;
+  int cap_batch = 0, seq = 0, mseq = 0;
+  int tmax0 = 0, tmax1 = 0;  // worst-case valid tokens before / after merge
+  int rows0 = 0, rows1 = 0;  // tmax rounded up to the GEMM M tile
+  cudaStream_t stream = nullptr;
+  // device buffers
+  uint32_t* ids = nullptr;
+  uint32_t* lengths = nullptr;
+  Meta* meta = nullptr;
+  uint32_t* err = nullptr;
+  float* rope = nullptr;
+  __half *x = nullptr, *norm = nullptr, *xm = nullptr, *nm = nullptr;
+  __half *qkv = nullptr, *q = nullptr, *k = nullptr, *attn = nullptr, *delta = nullptr;
+  __half *gu = nullptr, *ffn = nullptr;
+  float* out = nullptr;
+  // pinned host staging
+  uint32_t* h_ids = nullptr;
+  uint32_t* h_lengths = nullptr;
+  float* h_out = nullptr;
+  uint32_t* h_err = nullptr;
+  CUtensorMap map_norm0, map_norm1, map_attn, map_ffn;
+  int bn[kMaxLayers][4] = {};
+  cudaGraphExec_t graph_host = nullptr;    // H2D inputs -> forward -> D2H output
+  cudaGraphExec_t graph_device = nullptr;  // forward only
+  std::vector<void*> allocations;
+  int run_batch = 0;
+};
+
+struct Profile;
+struct Dump;
+int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, Dump* dump);
+void rope_table_host(int sequence, float* table);
+
+}  // namespace nemo
+
+struct nemo_model {
+  std::vector<std::unique_ptr<nemo::DeviceModel>> devs;
+  int n_layers = 0;
+  int vocab = 0;
+  int compact = 0;
+  int kquant = 0;
+  uint64_t packed_bytes = 0;
+};
+
+struct nemo_plan {
+  nemo_model* model = nullptr;
+  int batch = 0, seq = 0;
+  std::vector<std::unique_ptr<nemo::DevicePlan>> devs;
+};

@@ -1,0 +1,38 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares (no
+compute calls: runs without a GPU)."""
+import ctypes
+import os
+import re
+
+from conftest import REPO
+
+
+def declared_functions():
+    names = set()
+    for h in ("nemo.h", "nemo_ops.h"):
+        with open(os.path.join(REPO, "include", h)) as f:
+            text = f.read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(nemo_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    from nemo_b200 import runtime
+    lib = runtime.load_library()
+    names = declared_functions()
+    assert len(names) >= 20
+    for n in sorted(names):
+        assert hasattr(lib, n), n
+
+
+def test_host_only_entry_points():
+    from nemo_b200 import runtime
+    lib = runtime.load_library()
+    assert runtime.merged_length(5000) == 3200
+    assert lib.nemo_stage_name(0) == b"embedding_norm" and lib.nemo_stage_name(10) == b"pool"
+    import numpy as np
+    import oracle
+    t = np.zeros((7, 64, 2), np.float32)
+    assert lib.nemo_rope_table(7, t.ctypes.data_as(ctypes.c_void_p)) == 0
+    assert np.array_equal(t, oracle.rope_table(7))
