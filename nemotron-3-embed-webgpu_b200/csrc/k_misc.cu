@@ -93,7 +93,9 @@ __device__ void decode_group(int fmt, const uint8_t* __restrict__ src, int r, in
       const int hi = (blk[128 + half * 32 + j] >> (quad * 2)) & 3;
       const int qq = (lo | (hi << 4)) - 32;
       const int sc = (int)(int8_t)blk[192 + half * 8 + j / 16 + quad * 2];
-      v[j] = __fmul_rn(d, (float)(sc * qq));
+      // (d * scale) * q as the CPU decoder orders it: exact, and a zero keeps
+      // the sign of d * scale (quantization.ts:67-70).
+      v[j] = __fmul_rn(__fmul_rn(d, (float)sc), (float)qq);
     }
   } else {
     const uint8_t* blk;

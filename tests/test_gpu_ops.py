@@ -70,7 +70,8 @@ def test_embedding_bit_exact(rng):
     d_len, d_meta = meta_for(lengths, seq)
     t = __import__("torch")
     x = empty((3 * seq, 2048), t.float16)
-    check(L().nemo_op_embedding(ptr(dev(ids)), ptr(dev(table)), vocab, ptr(d_meta), 3 * seq, ptr(x)))
+    d_ids, d_table = dev(ids), dev(table)  # held: the kernel reads them after ptr() returns
+    check(L().nemo_op_embedding(ptr(d_ids), ptr(d_table), vocab, ptr(d_meta), 3 * seq, ptr(x)))
     packed = np.concatenate([ids[b, :n] for b, n in enumerate(lengths)])
     want = oracle.embedding(table, vocab, packed)
     got = host(x).view(np.uint16)[:packed.size]
@@ -88,7 +89,8 @@ def test_residual_rmsnorm(rng):
         dn = empty((rows, 2048), t.float16)
         d_rows = dev(np.array([rows], np.int32))
         dr = dev(residual.view(np.float16)) if residual is not None else None
-        check(L().nemo_op_rmsnorm(ptr(dx), ptr(dr) if dr is not None else None, ptr(dev(w)), ptr(dn), ptr(d_rows),
+        dw = dev(w)
+        check(L().nemo_op_rmsnorm(ptr(dx), ptr(dr) if dr is not None else None, ptr(dw), ptr(dn), ptr(d_rows),
                                   rows + 5))
         wx, wn = oracle.residual_rmsnorm(x, residual, w)
         assert np.array_equal(host(dx).view(np.uint16), wx)  # residual add is exact
@@ -105,7 +107,8 @@ def test_rope_bit_exact(rng):
     t = __import__("torch")
     q = empty((T, 3072), t.float16)
     k = empty((T, 1024), t.float16)
-    check(L().nemo_op_rope(ptr(dev(qkv.view(np.float16))), ptr(dev(table)), ptr(d_meta), 0, 2 * seq, ptr(q), ptr(k)))
+    d_qkv, d_table = dev(qkv.view(np.float16)), dev(table)
+    check(L().nemo_op_rope(ptr(d_qkv), ptr(d_table), ptr(d_meta), 0, 2 * seq, ptr(q), ptr(k)))
     pos = np.concatenate([np.arange(n) for n in lengths]).astype(np.int32)
     wq, wk = oracle.rope(qkv, pos, table)
     assert np.array_equal(host(q).view(np.uint16), wq)
@@ -117,7 +120,8 @@ def test_swiglu(rng):
     gu = f16_bits(rng.normal(0, 3, (rows, 12288)))
     t = __import__("torch")
     out = empty((rows, 6144), t.float16)
-    check(L().nemo_op_swiglu(ptr(dev(gu.view(np.float16))), ptr(dev(np.array([rows], np.int32))), rows, ptr(out)))
+    d_gu, d_rows = dev(gu.view(np.float16)), dev(np.array([rows], np.int32))
+    check(L().nemo_op_swiglu(ptr(d_gu), ptr(d_rows), rows, ptr(out)))
     assert ulp_diff(host(out).view(np.uint16), oracle.swiglu(gu)) <= 1
 
 
@@ -133,8 +137,8 @@ def test_merge_bit_exact(rng, lengths):
     t = __import__("torch")
     xm = empty((len(lengths) * mseq, 2048), t.float16)
     nm = empty((len(lengths) * mseq, 2048), t.float16)
-    check(L().nemo_op_merge(ptr(dev(x.view(np.float16))), ptr(dev(n.view(np.float16))), ptr(d_meta),
-                            len(lengths) * mseq, ptr(xm), ptr(nm)))
+    d_x, d_n = dev(x.view(np.float16)), dev(n.view(np.float16))
+    check(L().nemo_op_merge(ptr(d_x), ptr(d_n), ptr(d_meta), len(lengths) * mseq, ptr(xm), ptr(nm)))
     T1 = int(tgt.sum())
     assert np.array_equal(host(xm).view(np.uint16)[:T1], oracle.token_merge(x, lengths, tgt))
     assert np.array_equal(host(nm).view(np.uint16)[:T1], oracle.token_merge(n, lengths, tgt))
@@ -149,7 +153,8 @@ def test_mean_pool(rng):
     d_len, d_meta = meta_for(src, seq)
     t = __import__("torch")
     out = empty((3, 2048), t.float32)
-    check(L().nemo_op_pool(ptr(dev(x.view(np.float16))), ptr(d_meta), 3, ptr(out)))
+    d_x = dev(x.view(np.float16))
+    check(L().nemo_op_pool(ptr(d_x), ptr(d_meta), 3, ptr(out)))
     want = oracle.mean_pool(x, np.array(tgt, np.uint32))
     np.testing.assert_allclose(host(out), want, rtol=2e-5, atol=1e-7)
 
@@ -164,8 +169,8 @@ def test_attention(rng, lengths):
     d_len, d_meta = meta_for(lengths, seq)
     t = __import__("torch")
     out = empty((T, 3072), t.float16)
-    check(L().nemo_op_attention(ptr(dev(q.view(np.float16))), ptr(dev(k.view(np.float16))),
-                                ptr(dev(qkv.view(np.float16))), ptr(d_meta), 0, len(lengths), seq, ptr(out)))
+    d_q, d_k, d_qkv = dev(q.view(np.float16)), dev(k.view(np.float16)), dev(qkv.view(np.float16))
+    check(L().nemo_op_attention(ptr(d_q), ptr(d_k), ptr(d_qkv), ptr(d_meta), 0, len(lengths), seq, ptr(out)))
     want = oracle.attention(q, k, qkv, np.array(lengths, np.uint32))
     got = host(out).view(np.uint16)
     assert rel_err(f16_of_bits(got), f16_of_bits(want)) < 2e-3
@@ -184,8 +189,8 @@ def test_gemm(rng, m, impl_bn):
     w = f16_bits(rng.normal(0, 0.02, (n, k)))
     t = __import__("torch")
     y = empty((rows_pad, n), t.float16)
-    check(L().nemo_op_gemm(impl, ptr(dev(x.view(np.float16))), ptr(dev(w.view(np.float16))), ptr(y),
-                           ptr(dev(np.array([m], np.int32))), m, n, k, bn))
+    d_x, d_w, d_m = dev(x.view(np.float16)), dev(w.view(np.float16)), dev(np.array([m], np.int32))
+    check(L().nemo_op_gemm(impl, ptr(d_x), ptr(d_w), ptr(y), ptr(d_m), m, n, k, bn))
     ref32, ref16 = oracle.matmul_f16(x[:m], w)
     got = host(y).view(np.uint16)[:m]
     assert rel_err(f16_of_bits(got), ref32) < 2e-3
