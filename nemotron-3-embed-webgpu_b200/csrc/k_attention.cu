@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
   __shared__ __align__(16) __half qs[kQT][kHeadDim];
   __shared__ __align__(16) float ks[kKT][kHeadDim + 4];
   __shared__ __align__(16) float vs[kKT][kHeadDim];
+  dev::pdl_launch_dependents();  // lets the next projection start streaming its weights
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kQT;
   if (b >= meta->batch) return;
   const int* off = merged ? meta->tgt_off : meta->src_off;

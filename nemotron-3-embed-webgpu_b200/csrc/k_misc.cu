@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(__half* x, const __half* _
                                                       const float* __restrict__ w, __half* norm,
                                                       const int* __restrict__ d_rows, float eps) {
   __shared__ float red[32];
+  dev::pdl_launch_dependents();  // lets the next projection start streaming its weights
   const int row = blockIdx.x;
   if (row >= *d_rows) return;
   const int c = threadIdx.x * 8;

@@ -1,0 +1,473 @@
+// Fused-dequant projection GEMM for small token counts (T <= 64), the
+// batch-1 regime of the reference's latency/subgroup matmul pipelines
+// (src/webgpu/quant-matmul.ts:156-223,379-423, dispatched per
+// src/webgpu/model.ts:313-320). Here the projection is weight-bandwidth bound,
+// so the kernel streams the quantised bytes once and dequantises them on chip:
+//
+//   D[128 weight rows x NP tokens] += W_tile[128 x 16] . X^T[16 x NP]   (tcgen05, f16 in, f32 in TMEM)
+//
+// One CTA = one 128-row tile x one K range (split-K over the grid's y axis).
+//   warp 0      producer: starts streaming its packed weight chunks (one
+//               128-row x 256-column chunk per ring stage, cp.async.bulk)
+//               before waiting on the previous kernel, then TMA-loads the
+//               activation K range (box 64 x NP, 128B swizzle)
+//   warp 1      TMEM allocation + single-thread tcgen05.mma issue
+//   warps 2..5  decoders (thread = weight row): exact decode of the block
+//               with the reference's arithmetic (quantization.ts:19-74; every
+//               intermediate is exact or rounded once, as there), f16 round to
+//               nearest, written in the canonical 128B-swizzled K-major layout;
+//               then TMEM -> this CTA's partial tile in shared memory.
+// The split-K CTAs of one tile are one thread-block cluster: after a cluster
+// barrier each CTA reduces a slice of the tile's rows from its peers' shared
+// memory (DSMEM), summing the splits in rank order (deterministic), and applies
+// the fused epilogue (plain f16 store, RoPE + Q/K/V split, or SwiGLU).
+// All mbarrier waits are bounded (see common.cuh); every thread reaches both
+// cluster barriers on every path. Shared memory is sized per projection so
+// two CTAs share an SM when they fit.
+#include "kernels.cuh"
+
+namespace nemo {
+namespace {
+
+constexpr int kMaxRawStages = 3;
+constexpr int kAStages = 2;
+constexpr int kABytes = 128 * 128;  // 128 rows x 64 f16
+constexpr int kMaxSplits = 16;
+
+__device__ __forceinline__ float half_at(const uint8_t* p) {
+  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// --- packed f32x2 arithmetic (sm_100) ---------------------------------------
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return pack_h2(a, b);
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// 2^23 + n as f32 bits, for a small unsigned n.
+__device__ __forceinline__ float magic(uint32_t n) { return __uint_as_float(0x4B000000u | n); }
+
+__device__ __forceinline__ void st_chunk(uint8_t* a_tile, int r, int c, uint4 v) {
+  *reinterpret_cast<uint4*>(a_tile + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+__device__ __forceinline__ int region_bytes(int fmt) { return fmt == kSegQ6K ? 64 * 210 : 64 * 144; }
+
+// Q4_K row block (GGUF 144 B). Quarter q = elements 64q..64q+63 of the slab.
+// value = f32(d*sc*q - dmin*m) (quantization.ts:33-34): s = d*sc and
+// o = dmin*m are exact; fma(s, 2^23+q, -s*2^23) = s*q exactly; one rounding
+// in the subtraction of o, as in the reference.
+__device__ __forceinline__ void decode_q4k(const uint8_t* blk, int q, uint8_t* a_tile, int r) {
+  const float d = half_at(blk), dmin = half_at(blk + 2);
+  const uint8_t* s = blk + 4;
+  const int lo = 2 * q, hi = 2 * q + 1;
+  int sc_lo, m_lo, sc_hi, m_hi;
+  if (lo < 4) {
+    sc_lo = s[lo] & 63;
+    m_lo = s[lo + 4] & 63;
+    sc_hi = s[hi] & 63;
+    m_hi = s[hi + 4] & 63;
+  } else {
+    sc_lo = (s[lo + 4] & 15) | ((s[lo - 4] >> 6) << 4);
+    m_lo = (s[lo + 4] >> 4) | ((s[lo] >> 6) << 4);
+    sc_hi = (s[hi + 4] & 15) | ((s[hi - 4] >> 6) << 4);
+    m_hi = (s[hi + 4] >> 4) | ((s[hi] >> 6) << 4);
+  }
+  const float s_lo = __fmul_rn(d, (float)sc_lo), s_hi = __fmul_rn(d, (float)sc_hi);
+  const float o_lo = __fmul_rn(dmin, (float)m_lo), o_hi = __fmul_rn(dmin, (float)m_hi);
+  const float c_lo = -__fmul_rn(s_lo, 8388608.0f), c_hi = -__fmul_rn(s_hi, 8388608.0f);
+  const uint64_t S_lo = f2(s_lo, s_lo), S_hi = f2(s_hi, s_hi);
+  const uint64_t C_lo = f2(c_lo, c_lo), C_hi = f2(c_hi, c_hi);
+  const uint64_t O_lo = f2(-o_lo, -o_lo), O_hi = f2(-o_hi, -o_hi);
+  const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + q * 32);
+  const uint4 w0 = qv[0], w1 = qv[1];
+  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int sh = c < 4 ? 0 : 4;
+    const uint64_t S = c < 4 ? S_lo : S_hi, C = c < 4 ? C_lo : C_hi, O = c < 4 ? O_lo : O_hi;
+    const uint32_t wa = w[(c & 3) * 2], wb = w[(c & 3) * 2 + 1];
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t src = i < 2 ? wa : wb;
+      const int b0 = (i & 1) * 2;
+      const uint64_t qf = f2(magic((src >> (8 * b0 + sh)) & 15u), magic((src >> (8 * b0 + 8 + sh)) & 15u));
+      h[i] = f2_to_h2(fadd2(ffma2(S, qf, C), O));
+    }
+    st_chunk(a_tile, r, c, make_uint4(h[0], h[1], h[2], h[3]));
+  }
+}
+
+// Q6_K row block: ql[128] qh[64] scales[16] (208 B), d separate.
+// value = f32((d*sc) * (q - 32)) (quantization.ts:67-70): d*sc exact, q - 32
+// exact ((2^23+q) - (2^23+32)), one rounding in the product.
+__device__ __forceinline__ void decode_q6k(const uint8_t* blk, float d, int q, uint8_t* a_tile, int r) {
+  const int h = q >> 1, odd = q & 1;
+  const uint8_t* ql = blk + h * 64;
+  const uint8_t* qh = blk + 128 + h * 32;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + h * 8);
+  const uint4 l0 = reinterpret_cast<const uint4*>(ql)[0], l1 = reinterpret_cast<const uint4*>(ql)[1];
+  const uint4 l2 = reinterpret_cast<const uint4*>(ql)[2], l3 = reinterpret_cast<const uint4*>(ql)[3];
+  const uint4 h0 = reinterpret_cast<const uint4*>(qh)[0], h1 = reinterpret_cast<const uint4*>(qh)[1];
+  const uint32_t lw[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w, l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const int nsh = odd ? 4 : 0;
+  const uint64_t M32 = f2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int qi = c >> 2;
+    const int lane0 = (c & 3) * 8;
+    const int hsh = 4 * odd + 2 * qi;
+    const float ds = __fmul_rn(d, (float)sc[(2 * odd + qi) * 2 + lane0 / 16]);
+    const uint64_t DS = f2(ds, ds);
+    const uint32_t la = lw[qi * 8 + lane0 / 4], lb = lw[qi * 8 + lane0 / 4 + 1];
+    const uint32_t ha = hw[lane0 / 4], hb = hw[lane0 / 4 + 1];
+    uint32_t hv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t L = i < 2 ? la : lb, H = i < 2 ? ha : hb;
+      const int b0 = (i & 1) * 2;
+      const uint32_t qa = ((L >> (8 * b0 + nsh)) & 15u) | (((H >> (8 * b0 + hsh)) & 3u) << 4);
+      const uint32_t qb = ((L >> (8 * b0 + 8 + nsh)) & 15u) | (((H >> (8 * b0 + 8 + hsh)) & 3u) << 4);
+      hv[i] = f2_to_h2(fmul2(DS, fadd2(f2(magic(qa), magic(qb)), M32)));
+    }
+    st_chunk(a_tile, r, c, make_uint4(hv[0], hv[1], hv[2], hv[3]));
+  }
+}
+
+// Q4_0 row block for one 256 slab: d[8] (16 B) then 8 x 16 quant bytes.
+// value = f16(d * (q - 8)) (quantization.ts:42, quant-matmul.ts:106): computed
+// in f16x2: (1024 + q) - 1032 is exact and the f16 product rounds once to
+// nearest even, the same value as the exact f32 product rounded to f16.
+__device__ __forceinline__ void decode_q40(const uint8_t* blk, int q, uint8_t* a_tile, int r) {
+  const __half2 k1032 = __float2half2_rn(1032.0f);
+  const __half2 k16th = __float2half2_rn(0.0625f);
+  const __half2 k72 = __float2half2_rn(-72.0f);
+#pragma unroll
+  for (int bi = 0; bi < 2; ++bi) {
+    const int b = 2 * q + bi;
+    const __half dh = __ushort_as_half(*reinterpret_cast<const unsigned short*>(blk + 2 * b));
+    const __half2 d2 = __halves2half2(dh, dh);
+    const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + b * 16);
+    const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const bool high = cc >= 2;  // elements 16..31 are the high nibbles of bytes 0..15
+      const uint32_t wa = w[(cc & 1) * 2], wb = w[(cc & 1) * 2 + 1];
+      uint32_t hv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t src = i < 2 ? wa : wb;
+        const uint32_t pair = __byte_perm(src, 0, (i & 1) ? 0x4342u : 0x4140u);  // bytes -> low bytes of halves
+        __half2 qh;
+        if (!high) {
+          const uint32_t m = (pair & 0x000F000Fu) | 0x64006400u;  // 1024 + q
+          qh = __hsub2(*reinterpret_cast<const __half2*>(&m), k1032);
+        } else {
+          const uint32_t m = (pair & 0x00F000F0u) | 0x64006400u;  // 1024 + 16q
+          qh = __hfma2(*reinterpret_cast<const __half2*>(&m), k16th, k72);
+        }
+        const __half2 v = __hmul2(d2, qh);
+        hv[i] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      st_chunk(a_tile, r, bi * 4 + cc, make_uint4(hv[0], hv[1], hv[2], hv[3]));
+    }
+  }
+}
+
+__device__ __forceinline__ int find_req(const int* off, int batch, int tok) {
+  int b = 0;
+  while (b + 1 < batch && tok >= off[b + 1]) ++b;
+  return b;
+}
+
+template <int NP>
+__global__ void __launch_bounds__(192, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap map_x, SkinnyArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  dev::pdl_launch_dependents();
+  const uint32_t raw_s = dev::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int RS = a.rstages;
+  const int slab0 = split * a.slabs / a.splits, slab1 = (split + 1) * a.slabs / a.splits;
+  const int nsl = slab1 - slab0;
+  const int kr = nsl * 256;
+  // shared layout: X [kr/64][NP rows x 128 B] | raw ring | A ring | barriers
+  uint8_t* xs = smem;
+  uint8_t* raw = xs + (size_t)(a.slabs_max * 4) * NP * 128;
+  uint8_t* as = raw + ((RS * a.chunk_max + 1023) & ~1023);  // A tiles 1024-aligned (SW128)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(as + kAStages * kABytes);
+  const uint32_t xfull = dev::smem_u32(bars);
+  const uint32_t rfull = xfull + 8, rempty = rfull + 8 * kMaxRawStages;
+  const uint32_t afull = rempty + 8 * kMaxRawStages, aempty = afull + 8 * kAStages;
+  const uint32_t accum = aempty + 8 * kAStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 + 2 * kMaxRawStages + 2 * kAStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t kTmemCols = NP < 32 ? 32 : NP;
+  const SkinnyTile ti = a.tiles[tile];
+
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&map_x);
+    dev::mbar_init(xfull, 1);
+    for (int s = 0; s < kMaxRawStages; ++s) {
+      dev::mbar_init(rfull + 8 * s, 1);
+      dev::mbar_init(rempty + 8 * s, 128);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      dev::mbar_init(afull + 8 * s, 128);
+      dev::mbar_init(aempty + 8 * s, 1);
+    }
+    dev::mbar_init(accum, 1);
+    dev::fence_mbar_init();
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), kTmemCols);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint8_t* chunk0 = a.packed + ti.offset + (size_t)slab0 * ti.chunk_bytes;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Weights do not depend on the previous kernel: start streaming them
+      // before waiting for the activations (programmatic dependent launch).
+      int issued = 0;
+      for (int i = 0; i < nsl && i < RS; ++i) {
+        dev::mbar_arrive_expect_tx(rfull + 8 * i, ti.chunk_bytes);
+        dev::bulk_load(dev::smem_u32(raw + i * a.chunk_max), chunk0 + (size_t)i * ti.chunk_bytes, ti.chunk_bytes,
+                       rfull + 8 * i);
+        ++issued;
+      }
+      dev::pdl_wait();
+      dev::mbar_arrive_expect_tx(xfull, (uint32_t)(kr / 64) * NP * 128);
+      for (int c = 0; c < kr / 64; ++c)
+        dev::tma_load_2d(dev::smem_u32(xs + c * NP * 128), &map_x, slab0 * 256 + c * 64, 0, xfull);
+      for (int i = RS; i < nsl; ++i) {
+        const int s = i % RS;
+        if (!dev::mbar_wait(rempty + 8 * s, ((i / RS) & 1) ^ 1, a.err)) break;
+        dev::mbar_arrive_expect_tx(rfull + 8 * s, ti.chunk_bytes);
+        dev::bulk_load(dev::smem_u32(raw + s * a.chunk_max), chunk0 + (size_t)i * ti.chunk_bytes, ti.chunk_bytes,
+                       rfull + 8 * s);
+        ++issued;
+      }
+      // Drain: every issued copy has landed before shared memory is reused.
+      dev::mbar_wait(xfull, 0, a.err, 100000000ull);
+      for (int i = issued > RS ? issued - RS : 0; i < issued; ++i)
+        dev::mbar_wait(rfull + 8 * (i % RS), (i / RS) & 1, a.err, 100000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
+      if (dev::mbar_wait(xfull, 0, a.err)) {
+        const uint32_t xbase = dev::smem_u32(xs), abase = dev::smem_u32(as);
+        int sub = 0;
+        bool ok = true;
+        for (int i = 0; i < nsl && ok; ++i)
+          for (int q = 0; q < 4; ++q, ++sub) {
+            const int s = sub % kAStages;
+            if (!dev::mbar_wait(afull + 8 * s, (sub / kAStages) & 1, a.err)) {
+              ok = false;
+              break;
+            }
+            dev::tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = dev::make_sw128_desc(abase + s * kABytes + kk * 32);
+              const uint64_t bd = dev::make_sw128_desc(xbase + (i * 4 + q) * NP * 128 + kk * 32);
+              dev::tc_mma_f16(tmem, ad, bd, idesc, (sub | kk) != 0 ? 1u : 0u);
+            }
+            dev::tc_commit(aempty + 8 * s);
+          }
+      }
+      dev::tc_commit(accum);
+      dev::mbar_wait(accum, 0, a.err, 100000000ull);
+    }
+  } else {
+    // ---- decoders: thread = weight row of the tile ----
+    const int r = threadIdx.x - 64;
+    const int half = r >> 6, rr = r & 63;
+    const int fmt = ti.fmt[half];
+    const int roff = half ? region_bytes(ti.fmt[0]) : 0;
+    int sub = 0;
+    bool ok = true;
+    for (int i = 0; i < nsl && ok; ++i) {
+      const int rs = i % RS;
+      if (!dev::mbar_wait(rfull + 8 * rs, (i / RS) & 1, a.err)) break;
+      const uint8_t* region = raw + rs * a.chunk_max + roff;
+      const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
+      const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
+      for (int q = 0; q < 4; ++q, ++sub) {
+        const int s = sub % kAStages;
+        if (!dev::mbar_wait(aempty + 8 * s, ((sub / kAStages) & 1) ^ 1, a.err)) {
+          ok = false;
+          break;
+        }
+        uint8_t* a_tile = as + s * kABytes;
+        if (fmt == kSegQ4K) decode_q4k(blk, q, a_tile, r);
+        else if (fmt == kSegQ6K) decode_q6k(blk, d6, q, a_tile, r);
+        else decode_q40(blk, q, a_tile, r);
+        dev::fence_proxy_async_smem();
+        dev::mbar_arrive(afull + 8 * s);
+      }
+      dev::mbar_arrive(rempty + 8 * rs);
+    }
+    // ---- TMEM -> this CTA's partial tile in shared memory (red[t][row], f32;
+    // the raw ring is free once every chunk has been decoded) ----
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    float* red = reinterpret_cast<float*>(raw);
+    if (dev::mbar_wait(accum, 0, a.err)) {
+      dev::tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < NP; c0 += 16) {
+        uint32_t v[16];
+        dev::tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + c0, v);
+        dev::tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) red[(c0 + j) * 128 + row] = __uint_as_float(v[j]);
+      }
+    }
+  }
+  // ---- split-K reduction over the cluster + fused epilogue ----
+  dev::cluster_sync();
+  {
+    const int T = min(*a.d_tokens, NP);
+    const int S = a.splits, rank = split, n0 = tile * 128;
+    const uint32_t red_addr = dev::smem_u32(raw);
+    auto sum_row = [&](int t, int r) -> float {
+      const uint32_t local = red_addr + (uint32_t)(t * 128 + r) * 4u;
+      float v[kMaxSplits];
+#pragma unroll
+      for (int i = 0; i < kMaxSplits; ++i) v[i] = i < S ? dev::ld_dsmem_f32(dev::mapa(local, i)) : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxSplits; ++i)
+        if (i < S) acc = __fadd_rn(acc, v[i]);
+      return acc;
+    };
+    if (a.mode == kSkinnyPlain) {
+      const int r0 = rank * 128 / S, nr = (rank + 1) * 128 / S - r0;
+      for (int it = threadIdx.x; it < nr * T; it += blockDim.x) {
+        const int r = r0 + it % nr, t = it / nr;
+        a.out[(size_t)t * a.ldo + n0 + r] = __float2half_rn(sum_row(t, r));
+      }
+    } else if (a.mode == kSkinnyRope) {
+      const int* off = a.merged ? a.meta->tgt_off : a.meta->src_off;
+      const int p0 = rank * 64 / S, npairs = (rank + 1) * 64 / S - p0;
+      for (int it = threadIdx.x; it < npairs * T; it += blockDim.x) {
+        const int r = 2 * (p0 + it % npairs), t = it / npairs;
+        const int col = n0 + r;
+        // the reference stores QKV in f16 before rotating (ops.ts:189)
+        const float even = __half2float(__float2half_rn(sum_row(t, r)));
+        const float odd = __half2float(__float2half_rn(sum_row(t, r + 1)));
+        __half2 o;
+        if (col < kQWidth + kKVWidth) {
+          const int b = find_req(off, a.meta->batch, t);
+          const int pos = t - off[b];
+          const float2 cs = *reinterpret_cast<const float2*>(a.rope + ((size_t)pos * 64 + ((col & 127) >> 1)) * 2);
+          o = __halves2half2(__float2half_rn(__fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y))),
+                             __float2half_rn(__fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x))));
+          if (col < kQWidth) *reinterpret_cast<__half2*>(a.q + (size_t)t * kQWidth + col) = o;
+          else *reinterpret_cast<__half2*>(a.k + (size_t)t * kKVWidth + col - kQWidth) = o;
+        } else {
+          o = __halves2half2(__float2half_rn(even), __float2half_rn(odd));
+          *reinterpret_cast<__half2*>(a.out + (size_t)t * kQKVWidth + col) = o;
+        }
+      }
+    } else {
+      const int g0 = rank * 64 / S, ng = (rank + 1) * 64 / S - g0;
+      for (int it = threadIdx.x; it < ng * T; it += blockDim.x) {
+        const int r = g0 + it % ng, t = it / ng;
+        // gate/up stored f16 before SwiGLU (ops.ts:85-87)
+        const float g = __half2float(__float2half_rn(sum_row(t, r)));
+        const float u = __half2float(__float2half_rn(sum_row(t, r + 64)));
+        const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        a.out[(size_t)t * kInter + tile * 64 + r] = __float2half_rn(__fmul_rn(silu, u));
+      }
+    }
+  }
+  dev::cluster_sync();  // peers may still be reading this CTA's partial tile
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+size_t skinny_smem_bytes(int np, int slabs_max, int chunk_max, int rstages) {
+  return 1024 + (size_t)slabs_max * 4 * np * 128 + (((size_t)rstages * chunk_max + 1023) & ~(size_t)1023) +
+         kAStages * kABytes + 256;
+}
+
+cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np, int tiles, cudaStream_t s) {
+  if (a.splits < 1 || a.splits > kMaxSplits || a.splits > a.slabs || a.rstages < 2 || a.rstages > kMaxRawStages)
+    return cudaErrorInvalidValue;
+  const size_t smem = skinny_smem_bytes(np, a.slabs_max, a.chunk_max, a.rstages);
+  static bool configured[64][3] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const int ni = np == 16 ? 0 : np == 32 ? 1 : np == 64 ? 2 : -1;
+  if (ni < 0 || dev >= 64) return cudaErrorInvalidValue;
+  const void* fn = ni == 0 ? (const void*)skinny_kernel<16> : ni == 1 ? (const void*)skinny_kernel<32>
+                                                                       : (const void*)skinny_kernel<64>;
+  if (!configured[dev][ni]) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured[dev][ni] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, a.splits);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // the split-K CTAs of a tile
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = a.splits;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (ni == 0) return cudaLaunchKernelEx(&cfg, skinny_kernel<16>, *map_x, a);
+  if (ni == 1) return cudaLaunchKernelEx(&cfg, skinny_kernel<32>, *map_x, a);
+  return cudaLaunchKernelEx(&cfg, skinny_kernel<64>, *map_x, a);
+}
+
+}  // namespace nemo

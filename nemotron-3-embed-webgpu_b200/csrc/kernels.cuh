@@ -73,6 +73,45 @@ cudaError_t launch_gemm_tc(const CUtensorMap* map_a, const CUtensorMap* map_b, _
                            const int* d_rows, int max_rows, int n, int k, int bn, uint32_t* err,
                            cudaStream_t s);
 
+// --- fused-dequant split-K projection for T <= 64 tokens (k_skinny.cu) -----
+// Packed weights are re-tiled at load into 128-row tiles x 256-column slabs:
+// chunk(tile, slab) at packed + tile.offset + slab * tile.chunk_bytes holds two
+// 64-row regions (rows 0-63, 64-127), each in one format:
+//   Q4_K : 64 x 144 B GGUF blocks
+//   Q4_0 : 64 x [d[8] (16 B) | 8 x 16 quant bytes] (one 256 slab per row)
+//   Q6_K : 64 x [ql 128 | qh 64 | scales 16] (208 B), then 64 x f16 d
+struct SkinnyTile {
+  uint32_t offset;
+  uint32_t chunk_bytes;
+  uint8_t fmt[2];
+  uint8_t pad[6];
+};
+
+enum SkinnyMode { kSkinnyPlain = 0, kSkinnyRope = 1, kSkinnySwiglu = 2 };
+
+struct SkinnyArgs {
+  const uint8_t* packed;
+  const SkinnyTile* tiles;
+  uint32_t* err;
+  const int* d_tokens;
+  const Meta* meta;
+  int merged;
+  int n, slabs, splits, slabs_max, chunk_max;
+  int rstages;  // weight ring depth, 2 or 3
+  int mode;
+  __half* out;  // plain: [T x ldo]; rope: qkv buffer (V columns); swiglu: [T x 6144]
+  int ldo;
+  __half* q;
+  __half* k;
+  const float* rope;
+  int pdl;
+};
+
+size_t skinny_smem_bytes(int np, int slabs_max, int chunk_max, int rstages);
+// Grid (tiles, splits), cluster (1, splits) with splits <= 16 and <= slabs;
+// np = tokens padded to 16, 32 or 64; map_x box 64 x np.
+cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np, int tiles, cudaStream_t s);
+
 // Host: encodes a 2-D f16 tensor map over a row-major [outer x inner] array
 // with a (box_inner x box_outer) box and 128-byte swizzle.
 int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

@@ -6,6 +6,8 @@
 // token table, a small share of a B200's 180 GB.
 #include <string.h>
 
+#include <algorithm>
+
 #include "runtime.h"
 
 namespace nemo {
@@ -75,8 +77,102 @@ int resolve(const Pack& pack, int l, int which, std::vector<PartSpec>* parts, st
   return kOk;
 }
 
+// Builds the tile-slab image of one projection from its pack segments (host
+// bytes). Tile t holds matrix rows [128t, 128t+128), or for gate/up
+// (interleave) gate rows [64t, 64t+64) then up rows [n/2 + 64t, +64), so the
+// fused SwiGLU epilogue finds both halves of its outputs in one tile.
+int build_tile_slab(const uint8_t* file, const std::vector<PartSpec>& parts, int n, int k, bool interleave,
+                    TileSlabImage* img) {
+  struct HostSeg {
+    int fmt, row0, rows;
+    const uint8_t* data;
+  };
+  std::vector<HostSeg> segs;
+  int row0 = 0;
+  for (const PartSpec& ps : parts) {
+    segs.push_back({ps.fmt, row0, (int)ps.t->dims[1], file + ps.t->byte_offset});
+    row0 += (int)ps.t->dims[1];
+  }
+  if (n % 128 || k % 256) {
+    set_error("projection shape is not a multiple of the 128 x 256 tile");
+    return kErrFormat;
+  }
+  const int ntiles = n / 128, slabs = k / 256;
+  auto seg_of = [&](int row) -> const HostSeg* {
+    for (const HostSeg& s : segs)
+      if (row >= s.row0 && row < s.row0 + s.rows) return &s;
+    return nullptr;
+  };
+  auto tile_fmt = [](int segfmt) { return segfmt == kSegQ4K ? kSegQ4K : segfmt == kSegQ6K ? kSegQ6K : kSegQ40; };
+  auto region = [](int fmt) { return fmt == kSegQ6K ? 64 * 210 : 64 * 144; };
+  std::vector<int> base(ntiles * 2);
+  std::vector<const HostSeg*> tseg(ntiles * 2);
+  img->tiles.resize(ntiles);
+  uint64_t offset = 0;
+  img->chunk_max = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    for (int h = 0; h < 2; ++h) {
+      const int r = interleave ? (h == 0 ? t * 64 : n / 2 + t * 64) : t * 128 + 64 * h;
+      const HostSeg* s = seg_of(r);
+      if (!s || seg_of(r + 63) != s) {
+        set_error("projection segments must be aligned to 64-row groups");
+        return kErrFormat;
+      }
+      base[t * 2 + h] = r;
+      tseg[t * 2 + h] = s;
+      img->tiles[t].fmt[h] = (uint8_t)tile_fmt(s->fmt);
+    }
+    img->tiles[t].chunk_bytes = region(img->tiles[t].fmt[0]) + region(img->tiles[t].fmt[1]);
+    img->tiles[t].offset = (uint32_t)offset;
+    offset += (uint64_t)img->tiles[t].chunk_bytes * slabs;
+    img->chunk_max = std::max(img->chunk_max, (int)img->tiles[t].chunk_bytes);
+  }
+  if (offset >= (1ull << 32)) {
+    set_error("projection too large for 32-bit tile offsets");
+    return kErrFormat;
+  }
+  img->bytes.assign(offset, 0);
+  const int kb32 = k / 32;
+  for (int t = 0; t < ntiles; ++t)
+    for (int s = 0; s < slabs; ++s)
+      for (int h = 0; h < 2; ++h) {
+        const HostSeg& sg = *tseg[t * 2 + h];
+        const int fmt = img->tiles[t].fmt[h];
+        uint8_t* reg = img->bytes.data() + img->tiles[t].offset + (size_t)s * img->tiles[t].chunk_bytes +
+                       (h ? region(img->tiles[t].fmt[0]) : 0);
+        for (int rr = 0; rr < 64; ++rr) {
+          const int L = base[t * 2 + h] + rr - sg.row0;
+          if (sg.fmt == kSegQ4K) {
+            memcpy(reg + rr * 144, sg.data + ((size_t)L * slabs + s) * 144, 144);
+          } else if (sg.fmt == kSegQ6K) {
+            const uint8_t* src = sg.data + ((size_t)L * slabs + s) * 210;
+            memcpy(reg + rr * 208, src, 208);
+            memcpy(reg + 64 * 208 + rr * 2, src + 208, 2);
+          } else {
+            uint8_t* dst = reg + rr * 144;
+            for (int b = 0; b < 8; ++b) {
+              const uint8_t* blk;
+              const uint8_t* qs;
+              if (sg.fmt == kSegQ40) {
+                blk = sg.data + ((size_t)L * kb32 + s * 8 + b) * 18;
+                qs = blk + 2;
+              } else {  // q4_0-tile32-compact (format.ts:84-97)
+                blk = sg.data + ((((size_t)(L / 32)) * kb32 + s * 8 + b) * 32 + (L % 32)) * 20;
+                qs = blk + 4;
+              }
+              dst[2 * b] = blk[0];
+              dst[2 * b + 1] = blk[1];
+              memcpy(dst + 16 + b * 16, qs, 16);
+            }
+          }
+          (void)fmt;
+        }
+      }
+  return kOk;
+}
+
 int upload_replica(const uint8_t* file, const Pack& pack, int n_layers, int vocab, DeviceModel& dm,
-                   nemo_model* m, bool count) {
+                   nemo_model* m, bool count, const std::vector<TileSlabImage>& images) {
   NEMO_CUDA_TRY(cudaSetDevice(dm.device));
   const PackTensor& te = pack.tensors.at("token_embd.weight");
   if (dev_alloc(dm, &dm.embd, te.byte_length)) return kErrCuda;
@@ -125,6 +221,16 @@ int upload_replica(const uint8_t* file, const Pack& pack, int n_layers, int voca
       }
       for (int b = 0; b < kNumBn; ++b)
         if (int rc = make_tmap_f16(&pr.map[b], pr.w16, (uint64_t)pr.k, (uint64_t)pr.n, 64, kBnChoices[b])) return rc;
+      const TileSlabImage& img = images[l * 4 + which];
+      pr.tiles = (int)img.tiles.size();
+      pr.slabs = pr.k / 256;
+      pr.chunk_max = img.chunk_max;
+      pr.packed_bytes = img.bytes.size();
+      if (dev_alloc(dm, &pr.packed, img.bytes.size())) return kErrCuda;
+      NEMO_CUDA_TRY(cudaMemcpy(pr.packed, img.bytes.data(), img.bytes.size(), cudaMemcpyHostToDevice));
+      if (dev_alloc(dm, &pr.d_tiles, img.tiles.size() * sizeof(SkinnyTile))) return kErrCuda;
+      NEMO_CUDA_TRY(cudaMemcpy(pr.d_tiles, img.tiles.data(), img.tiles.size() * sizeof(SkinnyTile),
+                               cudaMemcpyHostToDevice));
     }
   }
   NEMO_CUDA_TRY(cudaDeviceSynchronize());
@@ -240,6 +346,22 @@ int model_load(const void* data, size_t bytes, const int* devices, int ndev, nem
       set_error("device " + std::to_string(d) + " is not present (" + std::to_string(count) + " devices)");
       return kErrArgs;
     }
+  // Tile-slab images for the small-T kernel: built once on the host, uploaded
+  // to every replica.
+  const uint8_t* file = reinterpret_cast<const uint8_t*>(data);
+  std::vector<TileSlabImage> images((size_t)n_layers * 4);
+  for (int l = 0; l < n_layers; ++l)
+    for (int which = 0; which < 4; ++which) {
+      std::vector<PartSpec> parts;
+      std::string perr;
+      if (resolve(pack, l, which, &parts, &perr)) {
+        set_error(perr);
+        return kErrFormat;
+      }
+      if (int rc = build_tile_slab(file, parts, kProjN[which], kProjK[which], which == kProjGateUp,
+                                   &images[l * 4 + which]))
+        return rc;
+    }
   auto* m = new nemo_model();
   m->n_layers = n_layers;
   m->vocab = vocab;
@@ -247,7 +369,7 @@ int model_load(const void* data, size_t bytes, const int* devices, int ndev, nem
     auto dm = std::make_unique<DeviceModel>();
     dm->device = devs[i];
     dm->vocab = vocab;
-    int rc = upload_replica(reinterpret_cast<const uint8_t*>(data), pack, n_layers, vocab, *dm, m, i == 0);
+    int rc = upload_replica(file, pack, n_layers, vocab, *dm, m, i == 0, images);
     m->devs.push_back(std::move(dm));
     if (rc) {
       for (auto& d : m->devs) free_replica(*d);

@@ -47,6 +47,34 @@ int pick_bn(int rows, int n) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// Split-K factor and weight-ring depth of the small-T kernel. The splits of a
+// tile form one cluster (at most 16 CTAs) and each needs >= 1 slab. Among the
+// choices that fit shared memory, pick the one whose grid fills the GPU's CTA
+// slots best in whole waves (two CTAs per SM when a CTA fits in half the SM's
+// shared memory), preferring the deeper ring, then fewer splits.
+void pick_splits(int tiles, int slabs, int np, int chunk_max, int* splits_out, int* rstages_out) {
+  double best = -1.0;
+  *splits_out = 1;
+  *rstages_out = 2;
+  for (int rs = 3; rs >= 2; --rs)
+    for (int s = 1; s <= std::min(slabs, 16); ++s) {
+      const size_t smem = skinny_smem_bytes(np, (slabs + s - 1) / s, chunk_max, rs);
+      const int per_sm = smem <= 113 * 1024 ? 2 : smem <= 226 * 1024 ? 1 : 0;
+      if (!per_sm) continue;
+      const int slots = 148 * per_sm;
+      const int ctas = tiles * s;
+      const int waves = (ctas + slots - 1) / slots;
+      // work per CTA ~ slabs/s; a wave costs the slowest CTA's slabs
+      const double time = waves * (double)((slabs + s - 1) / s) + 0.05 * s;
+      const double score = 1.0 / time;
+      if (score > best + 1e-9) {
+        best = score;
+        *splits_out = s;
+        *rstages_out = rs;
+      }
+    }
+}
+
 template <typename T>
 int plan_alloc(DevicePlan& p, T** ptr, size_t bytes) {
   void* v = nullptr;
@@ -115,25 +143,72 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     const int* rows = merged ? t1 : t0;
     const int maxr = merged ? p.tmax1 : p.tmax0;
     Projection* pr = dm.proj[l];
+    const int ph = merged ? 1 : 0;
+    const int np = p.np[ph];
+    // Small token counts: fused-dequant split-K kernel on the packed weights,
+    // with RoPE fused into QKV and SwiGLU into gate/up.
+    auto skinny = [&](int which, const CUtensorMap* xmap, int mode, __half* out, int ldo) -> int {
+      const Projection& P = pr[which];
+      SkinnyArgs a = {};
+      a.packed = P.packed;
+      a.tiles = P.d_tiles;
+      a.err = p.err;
+      a.d_tokens = rows;
+      a.meta = p.meta;
+      a.merged = merged ? 1 : 0;
+      a.n = P.n;
+      a.slabs = P.slabs;
+      a.splits = p.splits[l][which];
+      a.slabs_max = (P.slabs + a.splits - 1) / a.splits;
+      a.chunk_max = P.chunk_max;
+      a.rstages = p.rstages[l][which];
+      a.mode = mode;
+      a.out = out;
+      a.ldo = ldo;
+      a.q = p.q;
+      a.k = p.k;
+      a.rope = p.rope;
+      a.pdl = 1;
+      NEMO_LAUNCH(launch_skinny(xmap, a, np, P.tiles, s));
+      return kOk;
+    };
     stage(2);
-    NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth, kHidden,
-                               kBnChoices[p.bn[l][0]], p.err, s));
-    stage(3);
-    NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
+    if (np) {
+      if (int rc = skinny(kProjQKV, &p.xmap_norm[ph], kSkinnyRope, p.qkv, kQKVWidth)) return rc;
+      stage(3);
+    } else {
+      NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth,
+                                 kHidden, kBnChoices[p.bn[l][0]], p.err, s));
+      stage(3);
+      NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
+    }
     NEMO_LAUNCH(launch_attention(p.q, p.k, p.qkv, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, s));
     stage(4);
-    NEMO_LAUNCH(launch_gemm_tc(&p.map_attn, &pr[kProjO].map[p.bn[l][1]], p.delta, kHidden, rows, maxr, kHidden, kQWidth,
-                               kBnChoices[p.bn[l][1]], p.err, s));
+    if (np) {
+      if (int rc = skinny(kProjO, &p.xmap_attn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
+    } else {
+      NEMO_LAUNCH(launch_gemm_tc(&p.map_attn, &pr[kProjO].map[p.bn[l][1]], p.delta, kHidden, rows, maxr, kHidden,
+                                 kQWidth, kBnChoices[p.bn[l][1]], p.err, s));
+    }
     stage(5);
     NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, dm.ffn_norm[l], N, rows, maxr, s));
     stage(6);
-    NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjGateUp].map[p.bn[l][2]], p.gu, 2 * kInter, rows, maxr, 2 * kInter,
-                               kHidden, kBnChoices[p.bn[l][2]], p.err, s));
-    stage(7);
-    NEMO_LAUNCH(launch_swiglu(p.gu, rows, maxr, p.ffn, s));
+    if (np) {
+      if (int rc = skinny(kProjGateUp, &p.xmap_norm[ph], kSkinnySwiglu, p.ffn, kInter)) return rc;
+      stage(7);
+    } else {
+      NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjGateUp].map[p.bn[l][2]], p.gu, 2 * kInter, rows, maxr, 2 * kInter,
+                                 kHidden, kBnChoices[p.bn[l][2]], p.err, s));
+      stage(7);
+      NEMO_LAUNCH(launch_swiglu(p.gu, rows, maxr, p.ffn, s));
+    }
     stage(8);
-    NEMO_LAUNCH(launch_gemm_tc(&p.map_ffn, &pr[kProjDown].map[p.bn[l][3]], p.delta, kHidden, rows, maxr, kHidden,
-                               kInter, kBnChoices[p.bn[l][3]], p.err, s));
+    if (np) {
+      if (int rc = skinny(kProjDown, &p.xmap_ffn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
+    } else {
+      NEMO_LAUNCH(launch_gemm_tc(&p.map_ffn, &pr[kProjDown].map[p.bn[l][3]], p.delta, kHidden, rows, maxr, kHidden,
+                                 kInter, kBnChoices[p.bn[l][3]], p.err, s));
+    }
     stage(9);
     const float* next = l + 1 < n_layers ? dm.attn_norm[l + 1] : dm.output_norm;
     NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, next, N, rows, maxr, s));
@@ -239,6 +314,30 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, D
     const int rows = l >= kMergeAfterLayer ? p.rows1 : p.rows0;
     for (int w = 0; w < 4; ++w) p.bn[l][w] = pick_bn(rows, kProjN[w]);
   }
+  // Small-T path: worst-case tokens of the phase padded to the MMA N size.
+  const int tmax[2] = {p.tmax0, p.tmax1};
+  for (int ph = 0; ph < 2; ++ph) {
+    p.np[ph] = tmax[ph] <= 16 ? 16 : tmax[ph] <= 32 ? 32 : tmax[ph] <= 64 ? 64 : 0;
+    if (!p.np[ph]) continue;
+    if (make_tmap_f16(&p.xmap_norm[ph], ph ? (void*)p.nm : (void*)p.norm, kHidden, ph ? r1 : r0, 64, p.np[ph]) ||
+        make_tmap_f16(&p.xmap_attn[ph], p.attn, kQWidth, r0, 64, p.np[ph]) ||
+        make_tmap_f16(&p.xmap_ffn[ph], p.ffn, kInter, r0, 64, p.np[ph]))
+      return kErrCuda;
+  }
+  for (int l = 0; l < m->n_layers; ++l) {
+    const int ph = l >= kMergeAfterLayer ? 1 : 0;
+    if (!p.np[ph]) continue;
+    for (int w = 0; w < 4; ++w) {
+      const Projection& P = dm->proj[l][w];
+      pick_splits(P.tiles, P.slabs, p.np[ph], P.chunk_max, &p.splits[l][w], &p.rstages[l][w]);
+      if (skinny_smem_bytes(p.np[ph], (P.slabs + p.splits[l][w] - 1) / p.splits[l][w], P.chunk_max,
+                            p.rstages[l][w]) > 227 * 1024) {
+        set_error("small-T projection does not fit shared memory");
+        return kErrState;
+      }
+    }
+  }
+
   // The lengths buffer must hold a valid run before the first launch.
   NEMO_CUDA_TRY(cudaMemcpy(p.lengths, p.h_lengths, (size_t)(cap_batch + 1) * 4, cudaMemcpyHostToDevice));
   if (int rc = capture(p, m->n_layers, true, &p.graph_host)) return rc;

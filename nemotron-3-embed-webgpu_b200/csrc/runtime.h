@@ -33,6 +33,21 @@ struct Projection {
   __half* w16 = nullptr;     // effective f16 weights, [n x k] row-major
   CUtensorMap map[kNumBn];   // TMA maps over w16, box 64 x bn
   std::vector<Segment> segs;
+  // Tile-slab packed copy for the fused-dequant small-T kernel (k_skinny.cu).
+  // Gate/up tiles interleave 64 gate rows with the matching 64 up rows.
+  uint8_t* packed = nullptr;
+  SkinnyTile* d_tiles = nullptr;
+  int tiles = 0;
+  int slabs = 0;
+  int chunk_max = 0;
+  size_t packed_bytes = 0;
+};
+
+// Host-side tile-slab image of one projection, built once per model.
+struct TileSlabImage {
+  std::vector<uint8_t> bytes;
+  std::vector<SkinnyTile> tiles;
+  int chunk_max = 0;
 };
 
 struct DeviceModel {
@@ -73,6 +88,12 @@ struct DevicePlan {
   uint32_t* h_err = nullptr;
   CUtensorMap map_norm0, map_norm1, map_attn, map_ffn;
   int bn[kMaxLayers][4] = {};
+  // Small-T fused-dequant path: tokens padded to np (16/32/64) per phase
+  // (0 = layers 0-3, 1 = layers 4+); 0 selects the batched tcgen05 GEMM.
+  int np[2] = {0, 0};
+  CUtensorMap xmap_norm[2], xmap_attn[2], xmap_ffn[2];  // box 64 x np[phase]
+  int splits[kMaxLayers][4] = {};
+  int rstages[kMaxLayers][4] = {};
   cudaGraphExec_t graph_host = nullptr;    // H2D inputs -> forward -> D2H output
   cudaGraphExec_t graph_device = nullptr;  // forward only
   std::vector<void*> allocations;
