@@ -60,6 +60,13 @@ int nemo_op_rope(const void* d_qkv, const void* d_table, const void* d_meta, int
 int nemo_op_attention(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta,
                       int merged, int batch, int max_len, void* d_out);
 
+/* Same attention on the tcgen05 tensor cores (the kernel the plans run).
+ * d_q, d_k, d_qkv hold `rows` token rows (rows >= the metadata's token count);
+ * sampled layers (> 2048 valid keys) gather their keys into scratch buffers
+ * this call allocates. */
+int nemo_op_attention_tc(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta, int merged,
+                         int batch, int max_len, int rows, void* d_out);
+
 /* ops.ts:74-89: [rows x 12288] (gate | up) -> [rows x 6144]. */
 int nemo_op_swiglu(const void* d_gate_up, const void* d_rows, int max_rows, void* d_out);
 

@@ -181,6 +181,48 @@ int nemo_op_attention(const void* d_q, const void* d_k, const void* d_qkv, const
                                          (const Meta*)d_meta, merged != 0, batch, max_len, (__half*)d_out, 0));
 }
 
+int nemo_op_attention_tc(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta, int merged,
+                         int batch, int max_len, int rows, void* d_out) {
+  if (!d_q || !d_k || !d_qkv || !d_meta || !d_out || batch < 1 || batch > kMaxBatch || max_len < 1 || rows < 1) {
+    set_error("nemo_op_attention_tc: bad arguments");
+    return kErrArgs;
+  }
+  AttnMaps maps;
+  const int rows_c = rows / kSampleStride + batch + 1;
+  __half* kc = nullptr;
+  __half* vc = nullptr;
+  uint32_t* err = nullptr;
+  NEMO_CUDA_TRY(cudaMalloc(&kc, (size_t)rows_c * kKVWidth * 2));
+  NEMO_CUDA_TRY(cudaMalloc(&vc, (size_t)rows_c * kKVWidth * 2));
+  NEMO_CUDA_TRY(cudaMalloc(&err, 4));
+  NEMO_CUDA_TRY(cudaMemset(kc, 0, (size_t)rows_c * kKVWidth * 2));
+  NEMO_CUDA_TRY(cudaMemset(vc, 0, (size_t)rows_c * kKVWidth * 2));
+  NEMO_CUDA_TRY(cudaMemset(err, 0, 4));
+  int rc = kOk;
+  if (make_tmap_f16(&maps.q, d_q, kQWidth, rows, 64, 128) || make_tmap_f16(&maps.k, d_k, kKVWidth, rows, 64, 128) ||
+      make_tmap_f16(&maps.v, d_qkv, kQKVWidth, rows, 64, 128) ||
+      make_tmap_f16(&maps.kc, kc, kKVWidth, rows_c, 64, 128) || make_tmap_f16(&maps.vc, vc, kKVWidth, rows_c, 64, 128)) {
+    rc = kErrCuda;
+  } else {
+    rc = sync_and_check(launch_gather_sampled((const __half*)d_k, (const __half*)d_qkv, (const Meta*)d_meta,
+                                              merged != 0, rows_c, kc, vc, 0));
+    if (!rc)
+      rc = sync_and_check(
+          launch_attention_tc(maps, (const Meta*)d_meta, merged != 0, batch, max_len, (__half*)d_out, err, 0));
+  }
+  uint32_t h = 0;
+  cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost);
+  cudaFree(kc);
+  cudaFree(vc);
+  cudaFree(err);
+  if (rc) return rc;
+  if (h) {
+    set_error("tcgen05 attention: a bounded wait timed out");
+    return kErrTimeout;
+  }
+  return kOk;
+}
+
 int nemo_op_swiglu(const void* d_gate_up, const void* d_rows, int max_rows, void* d_out) {
   if (!d_gate_up || !d_rows || !d_out || max_rows < 1) {
     set_error("nemo_op_swiglu: bad arguments");

@@ -1,0 +1,332 @@
+// Bidirectional GQA flash attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM), the B200 counterpart of the reference's attention
+// pipelines (src/webgpu/ops.ts:213-293 tiled flash, :295-362 small).
+//
+// Semantics kept from the reference: each query of request b attends to the
+// request's valid keys of this layer; when that valid length exceeds 2048 only
+// every third key (positions 0, 3, 6, ...) is used (ops.ts:258-269) -- those
+// keys are gathered into a compact buffer first; queries at positions >= 16384
+// get the temperature factor of ops.ts:241; scale 1/sqrt(128); GQA q_head/3.
+// Scores and the softmax statistics are f32, P is rounded to f16 for the P.V
+// product (the reference keeps P in f16 as well), O accumulates in f32.
+//
+// One CTA = 128 queries of one q head of one request (192 threads):
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
+//               (double-buffered ring); V comes straight out of the QKV
+//               projection buffer and is consumed MN-major
+//   warp 1      TMEM allocation (512 columns: S ping-pong 2 x 128, O 128) and
+//               single-thread tcgen05.mma issue: S_j = Q.K_j^T, O += P_j.V_j
+//   warps 2..5  softmax (thread = query row): tcgen05.ld of the S row, online
+//               max/sum, P_j (f16) into 128B-swizzled shared memory, O row
+//               rescaled in TMEM (tcgen05.ld/st) when the running max moves;
+//               final O / l to global.
+// All mbarrier waits are bounded; on a timeout every role unwinds and TMEM is
+// released only after the CTA's MMAs have retired.
+#include "kernels.cuh"
+
+namespace nemo {
+namespace {
+
+constexpr int kTile = 128;
+constexpr int kHalfTile = kTile * 64 * 2;  // 128 rows x 64 f16 = 16 KB (one 128B-swizzle column block)
+constexpr int kTileBytes = 2 * kHalfTile;  // 128 x 128 f16
+constexpr int kSmem = 1024 + kTileBytes /*Q*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ + kTileBytes /*P*/ + 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 256;
+
+__device__ __forceinline__ void st_p_chunk(uint8_t* p_tile, int r, int c, uint4 v) {
+  // K-major 128B-swizzled: column block c/8 (64 keys), 16-byte chunk c%8.
+  uint8_t* blk = p_tile + (c >> 3) * kHalfTile;
+  const int cc = c & 7;
+  *reinterpret_cast<uint4*>(blk + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+}
+
+__device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct AttnTcArgs {
+  const Meta* meta;
+  int merged;
+  __half* out;
+  uint32_t* err;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_kc,
+                        const __grid_constant__ CUtensorMap map_vc, AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  dev::pdl_launch_dependents();
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kTile;
+  const Meta* meta = a.meta;
+  if (b >= meta->batch) return;
+  const int ph = a.merged ? 1 : 0;
+  const int len = a.merged ? meta->tgt_len[b] : meta->src_len[b];
+  if (q0 >= len) return;  // uniform over the CTA
+  const int base = a.merged ? meta->tgt_off[b] : meta->src_off[b];
+  const int kvh = h / (kQHeads / kKVHeads);
+  const bool sampled = len > kSampleThreshold;
+  const int nkeys = sampled ? (len + kSampleStride - 1) / kSampleStride : len;
+  const int kbase = sampled ? meta->samp_off[ph][b] : base;
+  const CUtensorMap* km = sampled ? &map_kc : &map_k;
+  const CUtensorMap* vm = sampled ? &map_vc : &map_v;
+  const int kcol = kvh * kHeadDim;
+  const int vcol = sampled ? kvh * kHeadDim : kQWidth + kKVWidth + kvh * kHeadDim;
+  const int ntiles = (nkeys + kTile - 1) / kTile;
+
+  const uint32_t raw_s = dev::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + 2 * kTileBytes;
+  uint8_t* sP = sV + 2 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  const uint32_t q_full = dev::smem_u32(bars);
+  const uint32_t kv_full = q_full + 8, kv_empty = kv_full + 16;
+  const uint32_t s_full = kv_empty + 16, p_ready = s_full + 16, pv_done = p_ready + 8;
+  const uint32_t mma_fin = pv_done + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&map_q);
+    dev::prefetch_tmap(km);
+    dev::prefetch_tmap(vm);
+    dev::mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      dev::mbar_init(kv_full + 8 * s, 1);
+      dev::mbar_init(kv_empty + 8 * s, 1);
+      dev::mbar_init(s_full + 8 * s, 1);
+    }
+    dev::mbar_init(p_ready, 128);
+    dev::mbar_init(pv_done, 1);
+    dev::mbar_init(mma_fin, 1);
+    dev::fence_mbar_init();
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), kTmemCols);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      dev::pdl_wait();
+      dev::mbar_arrive_expect_tx(q_full, kTileBytes);
+      dev::tma_load_2d(dev::smem_u32(sQ), &map_q, h * kHeadDim, base + q0, q_full);
+      dev::tma_load_2d(dev::smem_u32(sQ + kHalfTile), &map_q, h * kHeadDim + 64, base + q0, q_full);
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        if (!dev::mbar_wait(kv_empty + 8 * st, ((j >> 1) & 1) ^ 1, a.err)) break;
+        const uint32_t fb = kv_full + 8 * st;
+        dev::mbar_arrive_expect_tx(fb, 2 * kTileBytes);
+        const uint32_t dk = dev::smem_u32(sK + st * kTileBytes), dv = dev::smem_u32(sV + st * kTileBytes);
+        const int row = kbase + j * kTile;
+        dev::tma_load_2d(dk, km, kcol, row, fb);
+        dev::tma_load_2d(dk + kHalfTile, km, kcol + 64, row, fb);
+        dev::tma_load_2d(dv, vm, vcol, row, fb);
+        dev::tma_load_2d(dv + kHalfTile, vm, vcol + 64, row, fb);
+        ++issued;
+      }
+      dev::mbar_wait(q_full, 0, a.err, 100000000ull);
+      for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
+        dev::mbar_wait(kv_full + 8 * (i & 1), (i >> 1) & 1, a.err, 100000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = dev::make_idesc_f16(kTile, kTile);             // Q.K^T, both K-major
+      const uint32_t idesc_o = dev::make_idesc_f16(kTile, kHeadDim) | (1u << 16);  // P.V, V MN-major
+      const uint32_t aq = dev::smem_u32(sQ), ap = dev::smem_u32(sP);
+      bool ok = dev::mbar_wait(q_full, 0, a.err);
+      auto pv = [&](int i) -> bool {
+        if (!dev::mbar_wait(p_ready, i & 1, a.err)) return false;
+        dev::tc_fence_after();
+        const uint32_t bv = dev::smem_u32(sV + (i & 1) * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint64_t ad = dev::make_sw128_desc(ap + (kk >> 2) * kHalfTile + (kk & 3) * 32);
+          const uint64_t bd = dev::make_sw128_desc_mn(bv + kk * 2048, kHalfTile, 1024);
+          dev::tc_mma_f16(tmem + kColO, ad, bd, idesc_o, (i | kk) != 0 ? 1u : 0u);
+        }
+        dev::tc_commit(pv_done);
+        dev::tc_commit(kv_empty + 8 * (i & 1));
+        return true;
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j & 1;
+        if (!dev::mbar_wait(kv_full + 8 * st, (j >> 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        const uint32_t bk = dev::smem_u32(sK + st * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint64_t ad = dev::make_sw128_desc(aq + (kk >> 2) * kHalfTile + (kk & 3) * 32);
+          const uint64_t bd = dev::make_sw128_desc(bk + (kk >> 2) * kHalfTile + (kk & 3) * 32);
+          dev::tc_mma_f16(tmem + kColS + st * kTile, ad, bd, idesc_s, kk != 0 ? 1u : 0u);
+        }
+        dev::tc_commit(s_full + 8 * st);
+        if (j >= 1) ok = pv(j - 1);
+      }
+      if (ok) pv(ntiles - 1);
+      dev::tc_commit(mma_fin);
+      dev::mbar_wait(mma_fin, 0, a.err, 100000000ull);  // every MMA retired before TMEM is freed
+    }
+  } else {
+    // ---- softmax warps: thread = query row (TMEM lane) ----
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int pos = q0 + row;
+    const float temp = pos >= 16384 ? logf(floorf((float)pos / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
+    const float scale = 0.08838834764831845f * temp;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      // warp-uniform outcome: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(s_full + 8 * st, (j >> 1) & 1, a.err))) {
+        ok = false;
+        break;
+      }
+      dev::tc_fence_after();
+      float s[kTile];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        dev::tmem_ld_32x32b_x32(lane_base + kColS + st * kTile + c * 32, r);
+        dev::tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int valid = min(kTile, nkeys - j * kTile);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kTile; ++i) {
+        s[i] = i < valid ? s[i] * scale : -INFINITY;
+        tmax = fmaxf(tmax, s[i]);
+      }
+      const float mnew = fmaxf(m, tmax);
+      float rsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kTile; ++i) {
+        s[i] = __expf(s[i] - mnew);
+        rsum += s[i];
+      }
+      const float alpha = __expf(m - mnew);  // 0 on the first tile
+      if (j > 0) {
+        // PV_{j-1} complete: O is stable and the P buffer is free.
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(pv_done, (j - 1) & 1, a.err))) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            dev::tmem_ld_32x32b_x32(lane_base + kColO + c * 32, r);
+            dev::tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            dev::tmem_st_32x32b_x32(lane_base + kColO + c * 32, r);
+          }
+          dev::tc_wait_st();
+        }
+      }
+      l = l * alpha + rsum;
+      m = mnew;
+#pragma unroll
+      for (int c = 0; c < kTile / 8; ++c)
+        st_p_chunk(sP, row, c,
+                   make_uint4(pack_h2f(s[c * 8], s[c * 8 + 1]), pack_h2f(s[c * 8 + 2], s[c * 8 + 3]),
+                              pack_h2f(s[c * 8 + 4], s[c * 8 + 5]), pack_h2f(s[c * 8 + 6], s[c * 8 + 7])));
+      dev::fence_proxy_async_smem();
+      dev::tc_fence_before();
+      dev::mbar_arrive(p_ready);
+    }
+    if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done, (ntiles - 1) & 1, a.err))) {
+      dev::tc_fence_after();
+      const float inv = 1.0f / l;
+      __half* dst = a.out + (size_t)(base + pos) * kQWidth + h * kHeadDim;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        dev::tmem_ld_32x32b_x32(lane_base + kColO + c * 32, r);
+        dev::tc_wait_ld();
+        if (pos < len) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            reinterpret_cast<uint4*>(dst + c * 32)[v] =
+                make_uint4(pack_h2f(__uint_as_float(r[v * 8]) * inv, __uint_as_float(r[v * 8 + 1]) * inv),
+                           pack_h2f(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv),
+                           pack_h2f(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv),
+                           pack_h2f(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv));
+        }
+      }
+    }
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Gathers every third key of the requests whose valid length exceeds 2048
+// into compact K/V buffers (one 256-thread block per compact row).
+__global__ void __launch_bounds__(128) gather_sampled_kernel(const __half* __restrict__ k,
+                                                            const __half* __restrict__ qkv,
+                                                            const Meta* __restrict__ meta, int merged,
+                                                            __half* kc, __half* vc) {
+  const int ph = merged ? 1 : 0;
+  const int row = blockIdx.x;
+  if (row >= meta->samp_off[ph][meta->batch]) return;
+  int b = 0;
+  while (b + 1 < meta->batch && row >= meta->samp_off[ph][b + 1]) ++b;
+  const int base = merged ? meta->tgt_off[b] : meta->src_off[b];
+  const size_t src = (size_t)base + (size_t)(row - meta->samp_off[ph][b]) * kSampleStride;
+  const int c = threadIdx.x * 8;  // 128 threads x 8 = 1024 columns (8 kv heads x 128)
+  *reinterpret_cast<uint4*>(kc + (size_t)row * kKVWidth + c) =
+      *reinterpret_cast<const uint4*>(k + src * kKVWidth + c);
+  *reinterpret_cast<uint4*>(vc + (size_t)row * kKVWidth + c) =
+      *reinterpret_cast<const uint4*>(qkv + src * kQKVWidth + kQWidth + kKVWidth + c);
+}
+
+}  // namespace
+
+cudaError_t launch_gather_sampled(const __half* k, const __half* qkv, const Meta* meta, bool merged, int max_rows,
+                                  __half* kc, __half* vc, cudaStream_t s) {
+  if (max_rows <= 0) return cudaSuccess;
+  gather_sampled_kernel<<<max_rows, 128, 0, s>>>(k, qkv, meta, merged ? 1 : 0, kc, vc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
+                                __half* out, uint32_t* err, cudaStream_t s) {
+  if (max_len <= 0 || batch <= 0) return cudaSuccess;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  AttnTcArgs a{meta, merged ? 1 : 0, out, err};
+  dim3 grid((max_len + kTile - 1) / kTile, kQHeads, batch);
+  attention_tc_kernel<<<grid, 192, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
+  return cudaGetLastError();
+}
+
+}  // namespace nemo

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int quarter = warp & 3;
     const int row = m0 + quarter * 32 + lane;
-    if (dev::mbar_wait(accum, 0, err)) {
+    if (__all_sync(0xffffffffu, dev::mbar_wait(accum, 0, err))) {  // warp-uniform: tcgen05.ld is collective
       dev::tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {

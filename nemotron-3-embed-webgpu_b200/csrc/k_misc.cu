@@ -156,7 +156,7 @@ __global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const u
   meta->batch = batch;
   meta->seq = seq;
   meta->merged_seq = mseq;
-  int o0 = 0, o1 = 0;
+  int o0 = 0, o1 = 0, s0 = 0, s1 = 0;
   for (int b = 0; b < batch; ++b) {
     int l = (int)lengths[b];
     l = l < 1 ? 1 : (l > seq ? seq : l);
@@ -166,11 +166,17 @@ __global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const u
     meta->tgt_len[b] = t;
     meta->src_off[b] = o0;
     meta->tgt_off[b] = o1;
+    meta->samp_off[0][b] = s0;
+    meta->samp_off[1][b] = s1;
     o0 += l;
     o1 += t;
+    if (l > kSampleThreshold) s0 += (l + kSampleStride - 1) / kSampleStride;
+    if (t > kSampleThreshold) s1 += (t + kSampleStride - 1) / kSampleStride;
   }
   meta->src_off[batch] = o0;
   meta->tgt_off[batch] = o1;
+  meta->samp_off[0][batch] = s0;
+  meta->samp_off[1][batch] = s1;
   meta->t0 = o0;
   meta->t1 = o1;
 }

@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     float* red = reinterpret_cast<float*>(raw);
-    if (dev::mbar_wait(accum, 0, a.err)) {
+    if (__all_sync(0xffffffffu, dev::mbar_wait(accum, 0, a.err))) {  // warp-uniform: tcgen05.ld is collective
       dev::tc_fence_after();
 #pragma unroll
       for (int c0 = 0; c0 < NP; c0 += 16) {

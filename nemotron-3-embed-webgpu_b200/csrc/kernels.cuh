@@ -18,7 +18,13 @@ struct Meta {
   int tgt_len[kMaxBatch];
   int src_off[kMaxBatch + 1];
   int tgt_off[kMaxBatch + 1];
+  // Rows of the compact sampled K/V buffer per request and phase (requests
+  // whose valid length exceeds 2048 keep every third key, ops.ts:258-269).
+  int samp_off[2][kMaxBatch + 1];
 };
+
+constexpr int kSampleThreshold = 2048;
+constexpr int kSampleStride = 3;
 
 // Weight segment formats accepted by the decoders.
 enum SegFormat { kSegQ4K = 0, kSegQ6K = 1, kSegQ40 = 2, kSegQ40Tile32 = 3 };
@@ -49,6 +55,18 @@ cudaError_t launch_rope(const __half* qkv, const float* table, const Meta* meta,
 // 4096 (row stride 5120); out [T x 3072].
 cudaError_t launch_attention(const __half* q, const __half* k, const __half* qkv, const Meta* meta,
                              bool merged, int batch, int max_len, __half* out, cudaStream_t s);
+
+// tcgen05 flash attention (k_attention_tc.cu). Tensor maps (box 64 x 128,
+// 128B swizzle): q over Q [rows x 3072], k over K [rows x 1024], v over the
+// QKV buffer [rows x 5120] (V at column 4096), kc/vc over the compact sampled
+// K/V [rows_c x 1024] filled by launch_gather_sampled.
+struct AttnMaps {
+  CUtensorMap q, k, v, kc, vc;
+};
+cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
+                                __half* out, uint32_t* err, cudaStream_t s);
+cudaError_t launch_gather_sampled(const __half* k, const __half* qkv, const Meta* meta, bool merged, int max_rows,
+                                  __half* kc, __half* vc, cudaStream_t s);
 
 // ops.ts:74-89 over [rows x 12288] -> [rows x 6144].
 cudaError_t launch_swiglu(const __half* gate_up, const int* d_rows, int max_rows, __half* out,

@@ -182,7 +182,8 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
       stage(3);
       NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
     }
-    NEMO_LAUNCH(launch_attention(p.q, p.k, p.qkv, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, s));
+    if (p.gather[ph]) NEMO_LAUNCH(launch_gather_sampled(p.k, p.qkv, p.meta, merged, p.rows_c, p.kc, p.vc, s));
+    NEMO_LAUNCH(launch_attention_tc(p.amaps, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, p.err, s));
     stage(4);
     if (np) {
       if (int rc = skinny(kProjO, &p.xmap_attn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
@@ -309,6 +310,17 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, D
       make_tmap_f16(&p.map_norm1, p.nm, kHidden, r1, 64, kGemmTileM) ||
       make_tmap_f16(&p.map_attn, p.attn, kQWidth, r0, 64, kGemmTileM) ||
       make_tmap_f16(&p.map_ffn, p.ffn, kInter, r0, 64, kGemmTileM))
+    return kErrCuda;
+  // Attention: compact sampled K/V only when a phase can exceed 2048 keys.
+  p.gather[0] = p.seq > kSampleThreshold;
+  p.gather[1] = p.mseq > kSampleThreshold;
+  p.rows_c = (p.gather[0] || p.gather[1]) ? p.tmax0 / kSampleStride + cap_batch + 1 : kGemmTileM;
+  if (plan_alloc(p, &p.kc, (size_t)p.rows_c * kKVWidth * 2) || plan_alloc(p, &p.vc, (size_t)p.rows_c * kKVWidth * 2))
+    return kErrCuda;
+  if (make_tmap_f16(&p.amaps.q, p.q, kQWidth, r0, 64, 128) || make_tmap_f16(&p.amaps.k, p.k, kKVWidth, r0, 64, 128) ||
+      make_tmap_f16(&p.amaps.v, p.qkv, kQKVWidth, r0, 64, 128) ||
+      make_tmap_f16(&p.amaps.kc, p.kc, kKVWidth, p.rows_c, 64, 128) ||
+      make_tmap_f16(&p.amaps.vc, p.vc, kKVWidth, p.rows_c, 64, 128))
     return kErrCuda;
   for (int l = 0; l < m->n_layers; ++l) {
     const int rows = l >= kMergeAfterLayer ? p.rows1 : p.rows0;

@@ -92,6 +92,12 @@ struct DevicePlan {
   // (0 = layers 0-3, 1 = layers 4+); 0 selects the batched tcgen05 GEMM.
   int np[2] = {0, 0};
   CUtensorMap xmap_norm[2], xmap_attn[2], xmap_ffn[2];  // box 64 x np[phase]
+  // tcgen05 attention: maps over q / k / qkv and the compact sampled K/V
+  // (filled only for phases whose worst-case length exceeds 2048).
+  AttnMaps amaps;
+  __half *kc = nullptr, *vc = nullptr;
+  int rows_c = 0;
+  bool gather[2] = {false, false};
   int splits[kMaxLayers][4] = {};
   int rstages[kMaxLayers][4] = {};
   cudaGraphExec_t graph_host = nullptr;    // H2D inputs -> forward -> D2H output

@@ -159,8 +159,10 @@ def test_mean_pool(rng):
     np.testing.assert_allclose(host(out), want, rtol=2e-5, atol=1e-7)
 
 
-@pytest.mark.parametrize("lengths", [[15], [40, 3, 17], [2100, 300]], ids=["15", "ragged", "stride3"])
-def test_attention(rng, lengths):
+@pytest.mark.parametrize("impl", ["simt", "tcgen05"])
+@pytest.mark.parametrize("lengths", [[15], [40, 3, 17], [2100, 300], [129, 255, 1]],
+                         ids=["15", "ragged", "stride3", "tiles"])
+def test_attention(rng, lengths, impl):
     seq = max(lengths)
     T = sum(lengths)
     qkv = f16_bits(rng.normal(0, 1, (T, 5120)))
@@ -170,7 +172,11 @@ def test_attention(rng, lengths):
     t = __import__("torch")
     out = empty((T, 3072), t.float16)
     d_q, d_k, d_qkv = dev(q.view(np.float16)), dev(k.view(np.float16)), dev(qkv.view(np.float16))
-    check(L().nemo_op_attention(ptr(d_q), ptr(d_k), ptr(d_qkv), ptr(d_meta), 0, len(lengths), seq, ptr(out)))
+    if impl == "simt":
+        check(L().nemo_op_attention(ptr(d_q), ptr(d_k), ptr(d_qkv), ptr(d_meta), 0, len(lengths), seq, ptr(out)))
+    else:
+        check(L().nemo_op_attention_tc(ptr(d_q), ptr(d_k), ptr(d_qkv), ptr(d_meta), 0, len(lengths), seq, T,
+                                       ptr(out)))
     want = oracle.attention(q, k, qkv, np.array(lengths, np.uint32))
     got = host(out).view(np.uint16)
     assert rel_err(f16_of_bits(got), f16_of_bits(want)) < 2e-3
