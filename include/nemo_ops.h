@@ -67,6 +67,19 @@ int nemo_op_attention(const void* d_q, const void* d_k, const void* d_qkv, const
 int nemo_op_attention_tc(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta, int merged,
                          int batch, int max_len, int rows, void* d_out);
 
+/* nemo_op_attention_tc without any device allocation. No counterpart in the
+ * reference: it is for hosts that cannot call cudaMalloc/cudaFree where
+ * attention runs (device memory owned by another allocator or reserved up
+ * front; cudaFree would synchronise the whole device under a latency-bound
+ * server). Its scratch is one fixed device array of 8 MiB + 256 B per GPU,
+ * held until exit; calls needing more than 2048 sampled key rows (rows / 3 +
+ * batch + 1 when max_len > 2048) fail with NEMO_ERR_ARGS. All calls share the
+ * array: calls that overlap on the GPU race. The first call on a device looks
+ * up the array's address; make it before any stream capture. Same arguments
+ * and results as nemo_op_attention_tc. */
+int nemo_op_attention_tc_noalloc(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta, int merged,
+                                 int batch, int max_len, int rows, void* d_out);
+
 /* ops.ts:74-89: [rows x 12288] (gate | up) -> [rows x 6144]. */
 int nemo_op_swiglu(const void* d_gate_up, const void* d_rows, int max_rows, void* d_out);
 

@@ -75,6 +75,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_rope": (I, [P, P, P, I, I, P, P]),
         "nemo_op_attention": (I, [P, P, P, P, I, I, I, P]),
         "nemo_op_attention_tc": (I, [P, P, P, P, I, I, I, I, P]),
+        "nemo_op_attention_tc_noalloc": (I, [P, P, P, P, I, I, I, I, P]),
         "nemo_op_swiglu": (I, [P, P, I, P]),
         "nemo_op_merge": (I, [P, P, P, I, P, P]),
         "nemo_op_pool": (I, [P, P, I, P]),
