@@ -208,30 +208,22 @@ def run_reference(args) -> None:
 
 def run_ours(args) -> None:
     import torch
-    import torch.distributed as dist
 
+    from nemo_b200 import dist as ndist
     from nemo_b200 import synth
     from nemo_b200.runtime import NemotronB200Model
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rinfo = ndist.rank_info()
+    world, rank, local = rinfo.world, rinfo.rank, rinfo.local_rank
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    ndist.init("nccl", 300.0, torch.device("cuda", local))
 
     def barrier():
-        if world > 1:
-            dist.barrier()
+        ndist.barrier(rinfo)
         torch.cuda.synchronize()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return ndist.max_over_ranks(rinfo, v, "cuda")
 
     pack = synth.cached_model_pack(0, args.pack, 16)
     lengths = workload_lengths(args.workload, args.seed + rank)
@@ -262,7 +254,7 @@ def run_ours(args) -> None:
         barrier()
     ms = start.elapsed_time(end)
     ms_max = max_over_ranks(ms)
-    value = world * args.steps * batch / (ms_max / 1e3)
+    value = ndist.throughput(world, args.steps, batch, ms_max / 1e3)
 
     # --- end to end through the C ABI with host buffers (e2e) ----------------
     out = np.empty((batch, 2048), np.float32)
@@ -273,7 +265,7 @@ def run_ours(args) -> None:
     for _ in range(args.steps):
         plan.run_array(ids, lens, out)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e = world * args.steps * batch / e2e_s
+    e2e = ndist.throughput(world, args.steps, batch, e2e_s)
     h2d = ids.nbytes + (batch + 1) * 4
     d2h = out.nbytes + 4
 
@@ -307,9 +299,7 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_forward_rate(pack, lengths, args.seed, args.cpu_budget, None,
                                max_requests=1 if max(lengths) >= 500 else None)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ndist.shutdown(rinfo)
     if rank != 0:
         return
     line = {"metric": METRIC, "value": value, "unit": "req/s", "n_gpus": world, "steps": args.steps,

@@ -1,0 +1,34 @@
+"""Request sharding inside the C ABI: a model loaded on two devices splits each
+micro-batch's requests across them (longest first onto the least-loaded
+device); the embeddings must match the single-device run. Skipped with fewer
+than two GPUs."""
+import numpy as np
+import pytest
+
+from nemo_b200 import synth
+from nemo_b200.runtime import NemotronB200Model
+
+pytestmark = pytest.mark.gpu
+
+
+def test_two_device_plan_matches_single_device():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = synth.cached_model_pack(3, "kquant", 5)
+    with open(path, "rb") as f:
+        data = f.read()
+    reqs = synth.make_requests(8, [15, 40, 7, 33, 2], vocab=synth.VOCAB)
+    ids, lens, seq = synth.pad_batch(reqs)
+    one = NemotronB200Model(data, devices=[0])
+    two = NemotronB200Model(data, devices=[0, 1])
+    try:
+        assert two.info().n_devices == 2
+        a = one.create_plan(len(reqs), seq).run_array(ids, lens).copy()
+        b = two.create_plan(len(reqs), seq).run_array(ids, lens).copy()
+    finally:
+        one.destroy()
+        two.destroy()
+    for i in range(len(reqs)):
+        cos = float(a[i] @ b[i] / (np.linalg.norm(a[i]) * np.linalg.norm(b[i])))
+        assert cos >= 0.9999, (i, cos)
