@@ -23,7 +23,7 @@ extern "C" {
 #define NEMO_HIDDEN 2048       /* embedding width, src/webgpu/model.ts:19 */
 #define NEMO_MAX_BATCH 16      /* src/webgpu/embedding-engine.ts:37 */
 #define NEMO_MAX_SEQUENCE 32768
-#define NEMO_NUM_STAGES 11
+#define NEMO_NUM_STAGES 12
 
 typedef enum {
   NEMO_OK = 0,
@@ -93,6 +93,12 @@ int nemo_plan_run_device(nemo_plan* plan, const uint32_t* d_ids, const uint32_t*
 
 /* cudaStream_t of the plan's first device, as void*. */
 void* nemo_plan_stream(nemo_plan* plan);
+
+/* 1 when every device of the plan runs the forward as one persistent launch
+ * (plans whose batch x sequence is at most 16 tokens), 0 when it runs one
+ * kernel per op, NEMO_ERR_ARGS for a null plan. Build-specific introspection;
+ * the reference has no counterpart. */
+int nemo_plan_single_launch(nemo_plan* plan);
 
 /* Waits for the plan's streams; returns NEMO_ERR_TIMEOUT if a kernel reported
  * a bounded wait giving up. */

@@ -27,7 +27,7 @@ int plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint3
 int plan_run_debug(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
                    float* out, uint16_t* x_dump, uint16_t* norm_dump, int* tokens_per_layer);
 void rope_table_host(int sequence, float* table);
-extern const char* kStageNames[11];
+extern const char* kStageNames[12];
 
 namespace {
 int sync_and_check(cudaError_t launch) {
@@ -85,6 +85,16 @@ void* nemo_plan_stream(nemo_plan* plan) {
 }
 
 int nemo_plan_synchronize(nemo_plan* plan) { return plan_synchronize(plan); }
+
+int nemo_plan_single_launch(nemo_plan* plan) {
+  if (!plan || plan->devs.empty()) {
+    nemo::set_error("nemo_plan_single_launch: null plan");
+    return nemo::kErrArgs;
+  }
+  for (const auto& d : plan->devs)
+    if (!d->fgrid) return 0;
+  return 1;
+}
 
 int nemo_plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
                       float* stage_ms) {

@@ -1,0 +1,790 @@
+// Persistent single-launch encoder forward for small token counts (at most
+// kFwdNP valid tokens per run, the batch-1 regime of the reference's
+// latency-bound path: src/webgpu/model.ts:146-176 with the subgroup / latency
+// matmul pipelines of src/webgpu/quant-matmul.ts:156-223,379-423).
+//
+// At a handful of tokens every projection is a weight stream: ~33 MB of
+// quantised weights per layer against a few KB of activations. A launch per
+// op leaves the SMs idle between kernels and caps each projection at its own
+// pipeline fill. Here one cooperative grid (one CTA per SM) runs the whole
+// forward. Each CTA owns a fixed list of weight segments, (projection, 128-row
+// tile, K range of 256-column slabs), in forward order, and streams and
+// decodes them independently of the activations, running ahead across
+// layer boundaries as far as its rings allow. Only the tensor-core step waits
+// for activations.
+//
+//   warp 0      producer: cp.async.bulk of packed 128 x 256 weight chunks
+//               into a 3-stage ring, for all segments back to back
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
+//               D[128 rows x NP tokens] (+)= A[128 x 64] . X^T[64 x NP] per
+//               substage, D double-buffered in TMEM across segments
+//   warps 2-9   decoders (tile_decode.cuh): warps 2-5 fill substages 0 and 2
+//               of each slab, warps 6-9 substages 1 and 3, into an A ring
+//   warps 10-13 phase warps: the activation side of every phase
+//     - projection phases: stage X slabs (f16, 128B-swizzled) into an X
+//       ring, drain each finished segment from TMEM to an f32 partial slot in
+//       global memory, and count the tile's finished segments; the CTA that
+//       finishes a tile last sums its slots in K order (deterministic) and
+//       applies the epilogue: RoPE + Q/K/V split (QKV), f16 store (O, down)
+//       or SwiGLU (gate/up, rows interleaved 64 gate + 64 up per tile)
+//     - small phases: embedding + RMSNorm, attention, residual + RMSNorm,
+//       token merge, mean pool, each spread over the grid by item
+//   and a grid barrier between phases (release/acquire on a global counter).
+//
+// Every wait is bounded (%globaltimer) and also gives up as soon as any
+// thread has raised the error word, so a failure unwinds the whole grid
+// within microseconds; the host reads the word after the run. Loops of the
+// phase warps never exit early, so their named barriers always match.
+#include <math.h>
+
+#include "tile_decode.cuh"
+
+namespace nemo {
+namespace {
+
+using namespace tsd;
+
+constexpr int kThreads = 448;
+constexpr int kPhaseThread0 = 320;  // warps 10..13
+constexpr int kRawStages = 3;
+constexpr int kASlabs = 3;     // decoded A slabs in TMEM (128 x 256 f16 = 128 columns each)
+constexpr int kXStages = 4;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kLimitNs = 2000000000ull;
+constexpr uint32_t kDevErrGridBarrier = 4u;
+
+__device__ __forceinline__ uint32_t ld_err(const uint32_t* e) { return *reinterpret_cast<const volatile uint32_t*>(e); }
+
+// Bounded mbarrier wait that also returns false once the error word is set.
+__device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* err) {
+  if (dev::mbar_try_wait(bar, parity)) return true;
+  if (ld_err(err)) return false;
+  const uint64_t t0 = dev::globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (dev::mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (ld_err(err)) return false;
+      if (dev::globaltimer() - t0 > kLimitNs) {
+        atomicOr(err, kDevErrMbarTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void pw_sync() { dev::named_barrier(1, 128); }
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __halves2half2(__float2half_rn(v[2 * i]), __float2half_rn(v[2 * i + 1]));
+  return u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Row sum over 256 virtual threads (8 values each) with the reduction tree of
+// the 256-thread row kernels in k_misc.cu (butterfly per 32 virtual lanes,
+// then a butterfly over the 8 warp totals): phase thread p holds virtual
+// threads p (s0) and 128 + p (s1), so the result is bit-identical.
+__device__ __forceinline__ float row_sum_256(float s0, float s1, float* red) {
+  const int pt = threadIdx.x - kPhaseThread0, w = pt >> 5, lane = pt & 31;
+  s0 = warp_sum(s0);
+  s1 = warp_sum(s1);
+  if (lane == 0) {
+    red[w] = s0;
+    red[4 + w] = s1;
+  }
+  pw_sync();
+  float t = lane < 8 ? red[lane] : 0.f;
+  t = warp_sum(t);
+  pw_sync();  // red is reused by the next call
+  return t;
+}
+
+struct Shared {
+  uint32_t tmem;
+  int flag;
+  float red[8];
+};
+
+template <int NP>
+__global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_constant__ FwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = dev::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  constexpr int kXBytes = 4 * NP * 128;      // one 256-column slab of X: 4 x [NP rows x 64 f16]
+  constexpr int kSlotBytes = NP * 128 * 4;   // one partial-sum slot: [NP][128] f32
+  const int CM = a.chunk_max;
+  // shared layout: X ring | epilogue slots | raw weight ring | barriers
+  uint8_t* xring = smem;
+  float* ebuf = reinterpret_cast<float*>(xring + kXStages * kXBytes);
+  uint8_t* raw = reinterpret_cast<uint8_t*>(ebuf) + (size_t)a.max_slots * kSlotBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + ((kRawStages * CM + 15) & ~15));
+  const uint32_t rfull = dev::smem_u32(bars), rempty = rfull + 8 * kRawStages;
+  const uint32_t afull = rempty + 8 * kRawStages, aempty = afull + 8 * kASlabs;
+  const uint32_t xfull = aempty + 8 * kASlabs, xempty = xfull + 8 * kXStages;
+  const uint32_t dfull = xempty + 8 * kXStages, dempty = dfull + 16, fin = dempty + 16, ebar = fin + 8;
+  Shared* sh = reinterpret_cast<Shared*>(bars + 2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+  const FwdSeg* segs = a.segs + a.seg_start[cta];
+  const int nseg = a.seg_start[cta + 1] - a.seg_start[cta];
+  uint32_t* err = a.err;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 4; ++i) dev::prefetch_tmap(&a.xmap[i]);
+    for (int s = 0; s < kRawStages; ++s) {
+      dev::mbar_init(rfull + 8 * s, 1);
+      dev::mbar_init(rempty + 8 * s, 256);
+    }
+    for (int s = 0; s < kASlabs; ++s) {
+      dev::mbar_init(afull + 8 * s, 256);
+      dev::mbar_init(aempty + 8 * s, 1);
+    }
+    for (int s = 0; s < kXStages; ++s) {
+      dev::mbar_init(xfull + 8 * s, 1);
+      dev::mbar_init(xempty + 8 * s, 1);
+    }
+    for (int d = 0; d < 2; ++d) {
+      dev::mbar_init(dfull + 8 * d, 1);
+      dev::mbar_init(dempty + 8 * d, 128);
+    }
+    dev::mbar_init(fin, 1);
+    dev::mbar_init(ebar, 1);
+    dev::fence_mbar_init();
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(&sh->tmem), kTmemCols);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = sh->tmem;
+  // TMEM columns: two D buffers (segments alternate), each two accumulators
+  // (even / odd substages: independent MMA chains) of NP columns, then the A
+  // slabs.
+  const uint32_t tm_a = tmem + 4 * NP;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int si = 0; si < nseg && ok; ++si) {
+        const FwdSeg sg = segs[si];
+        const FwdProj P = a.proj[sg.proj];
+        const SkinnyTile ti = P.tiles[sg.tile];
+        const uint8_t* src = P.packed + ti.offset;
+        for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
+          const int s = it % kRawStages;
+          if (!wait(rempty + 8 * s, ((it / kRawStages) & 1) ^ 1, err)) {
+            ok = false;
+            break;
+          }
+          dev::mbar_arrive_expect_tx(rfull + 8 * s, ti.chunk_bytes);
+          dev::bulk_load(dev::smem_u32(raw + s * CM), src + (size_t)sl * ti.chunk_bytes, ti.chunk_bytes,
+                         rfull + 8 * s);
+        }
+      }
+      // Every issued copy lands before the CTA may exit.
+      for (int j = it > kRawStages ? it - kRawStages : 0; j < it; ++j)
+        dev::mbar_wait(rfull + 8 * (j % kRawStages), (j / kRawStages) & 1, err, 100000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
+      const uint32_t xbase = dev::smem_u32(xring);
+      int it = 0;
+      bool ok = true;
+      for (int si = 0; si < nseg && ok; ++si) {
+        const FwdSeg sg = segs[si];
+        const int d = si & 1;
+        if (!wait(dempty + 8 * d, ((si >> 1) & 1) ^ 1, err)) break;
+        dev::tc_fence_after();
+        for (int sl = sg.s0; sl < sg.s1 && ok; ++sl, ++it) {
+          const int xs = it % kXStages;
+          if (!wait(xfull + 8 * xs, (it / kXStages) & 1, err)) {
+            ok = false;
+            break;
+          }
+          const int s = it % kASlabs;
+          if (!wait(afull + 8 * s, (it / kASlabs) & 1, err)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bd = dev::make_sw128_desc(xbase + xs * kXBytes + q * NP * 128 + kk * 32);
+              dev::tc_mma_f16_ts(tmem + (2 * d + (q & 1)) * NP, tm_a + s * 128 + q * 32 + kk * 8, bd, idesc,
+                                 (sl != sg.s0 || q >= 2 || kk != 0) ? 1u : 0u);
+            }
+          dev::tc_commit(aempty + 8 * s);
+          dev::tc_commit(xempty + 8 * xs);
+        }
+        if (ok) dev::tc_commit(dfull + 8 * d);
+      }
+      // All issued MMAs complete before the TMEM is released.
+      dev::tc_commit(fin);
+      dev::mbar_wait(fin, 0, err, 100000000ull);
+    }
+  } else if (threadIdx.x < kPhaseThread0) {
+    // ------------------------------------------------------------ decoders
+    // Warp w writes TMEM lanes 32 * (w % 4) .. + 31, so its threads own those
+    // weight rows; warps 2-5 fill substages 0 and 2 of every slab, warps 6-9
+    // substages 1 and 3. A slab is handed to the MMA once both halves are in.
+    const int quarter = warp & 3, grp = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const int half = r >> 6, rr = r & 63;  // half is uniform within a warp
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    int it = 0;
+    bool ok = true;
+    for (int si = 0; si < nseg && ok; ++si) {
+      const FwdSeg sg = segs[si];
+      const SkinnyTile ti = a.proj[sg.proj].tiles[sg.tile];
+      const int fmt = ti.fmt[half];
+      const int roff = half ? region_bytes(ti.fmt[0]) : 0;
+      for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
+        const int rs = it % kRawStages;
+        if (!__all_sync(0xffffffffu, wait(rfull + 8 * rs, (it / kRawStages) & 1, err))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* region = raw + rs * CM + roff;
+        const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
+        const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
+        const int s = it % kASlabs;
+        if (!__all_sync(0xffffffffu, wait(aempty + 8 * s, ((it / kASlabs) & 1) ^ 1, err))) {
+          ok = false;
+          break;
+        }
+#pragma unroll 1
+        for (int qq = 0; qq < 2; ++qq) {
+          const int q = grp + 2 * qq;
+          uint32_t h[32];
+          const RegSink sink{h};
+          if (fmt == kSegQ4K) decode_q4k(blk, q, sink);
+          else if (fmt == kSegQ6K) decode_q6k(blk, d6, q, sink);
+          else decode_q40(blk, q, sink);
+          dev::tmem_st_32x32b_x32(tm_a + lane_base + s * 128 + q * 32, h);
+        }
+        dev::tc_wait_st();
+        dev::tc_fence_before();
+        dev::mbar_arrive(afull + 8 * s);
+        dev::mbar_arrive(rempty + 8 * rs);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ phase warps
+    const int pt = threadIdx.x - kPhaseThread0;
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const Meta* meta = a.meta;
+    const int batch = min(meta->batch, kMaxBatch);
+    const int T0 = min(meta->t0, NP), T1 = min(meta->t1, NP);
+    int si = 0, xit = 0, gseg = 0, eph = 0;
+    uint32_t nbar = 0;
+
+    auto grid_barrier = [&]() {
+      pw_sync();
+      if (pt == 0) {
+        __threadfence();
+        atomicAdd(&a.sync[0], 1u);
+        const uint32_t target = (++nbar) * (uint32_t)G;
+        if (!ld_err(err)) {
+          const uint64_t t0 = dev::globaltimer();
+          for (uint32_t i = 0;; ++i) {
+            if (ld_acquire(&a.sync[0]) >= target) break;
+            if ((i & 15u) == 15u) {
+              if (ld_err(err)) break;
+              if (dev::globaltimer() - t0 > kLimitNs) {
+                atomicOr(err, kDevErrGridBarrier);
+                break;
+              }
+            }
+          }
+        }
+        __threadfence();
+        // X tiles of the next phase are read by TMA (async proxy) after this.
+        dev::fence_proxy_async_global();
+      }
+      pw_sync();
+    };
+
+    // Split-K epilogue of a finished tile: one bulk copy brings all of its
+    // partial slots (written by other CTAs, released through the tile counter)
+    // into shared memory; they are summed in slot (= K) order.
+    auto epilogue = [&](int pi, int tile, int T, bool merged) {
+      const int S = a.nslots[pi * kFwdMaxTiles + tile];
+      if (pt == 0) {
+        dev::fence_proxy_async_global();
+        dev::mbar_arrive_expect_tx(ebar, (uint32_t)(S * kSlotBytes));
+        dev::bulk_load(dev::smem_u32(ebuf), a.part + (size_t)tile * a.max_slots * (kSlotBytes / 4),
+                       (uint32_t)(S * kSlotBytes), ebar);
+      }
+      const bool got = wait(ebar, eph & 1, err);
+      ++eph;
+      const int which = pi & 3, n0 = tile * 128;
+      // Each thread keeps one accumulator per token (independent chains) and
+      // adds the slots in order.
+      if (got && which == 0) {  // QKV: the reference stores f16 QKV, then rotates Q and K (ops.ts:168-194)
+        const int r = 2 * (pt & 63), tb = (pt >> 6) * (NP / 2);
+        float e[NP / 2], o[NP / 2];
+#pragma unroll
+        for (int j = 0; j < NP / 2; ++j) e[j] = o[j] = 0.f;
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+          for (int j = 0; j < NP / 2; ++j) {
+            const float2 v = *reinterpret_cast<const float2*>(ebuf + (s * NP + tb + j) * 128 + r);
+            e[j] = __fadd_rn(e[j], v.x);
+            o[j] = __fadd_rn(o[j], v.y);
+          }
+        const int col = n0 + r;
+        const int* off = merged ? meta->tgt_off : meta->src_off;
+#pragma unroll
+        for (int j = 0; j < NP / 2; ++j) {
+          const int t = tb + j;
+          if (t >= T) break;
+          const float even = __half2float(__float2half_rn(e[j])), odd = __half2float(__float2half_rn(o[j]));
+          if (col < kQWidth + kKVWidth) {
+            const int b = find_req(off, batch, t);
+            const int pos = t - off[b];
+            const float2 cs = *reinterpret_cast<const float2*>(a.rope + ((size_t)pos * 64 + ((col & 127) >> 1)) * 2);
+            const __half2 h = __halves2half2(__float2half_rn(__fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y))),
+                                             __float2half_rn(__fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x))));
+            if (col < kQWidth) *reinterpret_cast<__half2*>(a.q + (size_t)t * kQWidth + col) = h;
+            else *reinterpret_cast<__half2*>(a.k + (size_t)t * kKVWidth + col - kQWidth) = h;
+          } else {
+            *reinterpret_cast<__half2*>(a.qkv + (size_t)t * kQKVWidth + col) =
+                __halves2half2(__float2half_rn(even), __float2half_rn(odd));
+          }
+        }
+      } else if (got && which == 2) {  // gate/up: f16 gate and up, then SwiGLU (ops.ts:74-89)
+        const int r = pt & 63, tb = (pt >> 6) * (NP / 2);
+        float g[NP / 2], u[NP / 2];
+#pragma unroll
+        for (int j = 0; j < NP / 2; ++j) g[j] = u[j] = 0.f;
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+          for (int j = 0; j < NP / 2; ++j) {
+            const float* p = ebuf + (s * NP + tb + j) * 128;
+            g[j] = __fadd_rn(g[j], p[r]);
+            u[j] = __fadd_rn(u[j], p[64 + r]);
+          }
+#pragma unroll
+        for (int j = 0; j < NP / 2; ++j) {
+          const int t = tb + j;
+          if (t >= T) break;
+          const float gh = __half2float(__float2half_rn(g[j])), uh = __half2float(__float2half_rn(u[j]));
+          const float silu = __fdiv_rn(gh, __fadd_rn(1.0f, expf(-gh)));
+          a.ffn[(size_t)t * kInter + tile * 64 + r] = __float2half_rn(__fmul_rn(silu, uh));
+        }
+      } else if (got) {  // O and down: f16 delta
+        float acc[NP];
+#pragma unroll
+        for (int t = 0; t < NP; ++t) acc[t] = 0.f;
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+          for (int t = 0; t < NP; ++t) acc[t] = __fadd_rn(acc[t], ebuf[(s * NP + t) * 128 + pt]);
+#pragma unroll
+        for (int t = 0; t < NP; ++t)
+          if (t < T) a.delta[(size_t)t * kHidden + n0 + pt] = __float2half_rn(acc[t]);
+      }
+      dev::fence_proxy_async_smem();  // these reads of ebuf precede the next bulk write into it
+      pw_sync();
+    };
+
+    // TMEM -> partial slot; the CTA that completes the tile runs its epilogue.
+    auto drain = [&](const FwdSeg& sg, int T, bool merged) {
+      const int d = gseg & 1;
+      const bool got = __all_sync(0xffffffffu, wait(dfull + 8 * d, (gseg >> 1) & 1, err));
+      ++gseg;
+      float* slot = a.part + ((size_t)sg.tile * a.max_slots + sg.slot) * (kSlotBytes / 4);
+      if (got) {
+        dev::tc_fence_after();
+        const int row = quarter * 32 + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < NP; c0 += 16) {
+          uint32_t v0[16], v1[16];
+          const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * d * NP + c0;
+          dev::tmem_ld_32x32b_x16(base, v0);
+          dev::tmem_ld_32x32b_x16(base + NP, v1);
+          dev::tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < T) __stcg(slot + (c0 + j) * 128 + row, __uint_as_float(v0[j]) + __uint_as_float(v1[j]));
+        }
+      }
+      dev::tc_fence_before();
+      dev::mbar_arrive(dempty + 8 * d);
+      pw_sync();
+      if (pt == 0) {
+        int last = 0;
+        if (!ld_err(err)) {
+          __threadfence();
+          const int idx = sg.proj * kFwdMaxTiles + sg.tile;
+          const uint32_t old = atomicAdd(&a.sync[1 + idx], 1u);
+          last = old + 1 == (uint32_t)a.nslots[idx];
+          if (last) __threadfence();
+        }
+        sh->flag = last;
+      }
+      pw_sync();
+      if (*reinterpret_cast<volatile int*>(&sh->flag)) epilogue(sg.proj, sg.tile, T, merged);
+    };
+
+    // X slabs by TMA (thread 0), then drains of the finished segments.
+    auto projection = [&](int pi, const CUtensorMap* xmap, bool merged) {
+      const int T = merged ? T1 : T0;
+      const int first = si;
+      while (si < nseg && segs[si].proj == pi) ++si;
+      for (int j = first; j < si; ++j) {
+        const FwdSeg sg = segs[j];
+        if (pt == 0) {
+          for (int sl = sg.s0; sl < sg.s1; ++sl, ++xit) {
+            const int xs = xit % kXStages;
+            if (wait(xempty + 8 * xs, ((xit / kXStages) & 1) ^ 1, err)) {
+              dev::mbar_arrive_expect_tx(xfull + 8 * xs, kXBytes);
+              for (int q = 0; q < 4; ++q)
+                dev::tma_load_2d(dev::smem_u32(xring + xs * kXBytes + q * NP * 128), xmap, sl * 256 + q * 64, 0,
+                                 xfull + 8 * xs);
+            }
+          }
+        }
+        if (j > first) drain(segs[j - 1], T, merged);
+      }
+      if (si > first) drain(segs[si - 1], T, merged);
+    };
+
+    // residual add (optional) + RMSNorm of one row (ops.ts:21-72).
+    auto norm_row = [&](__half* x, const __half* res, const float* w, __half* out, int t) {
+      float v[2][8];
+      float ss[2] = {0.f, 0.f};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = h * 1024 + pt * 8;
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(x + (size_t)t * kHidden + c)), v[h]);
+        if (res) {
+          float r8[8];
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(res + (size_t)t * kHidden + c)), r8);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[h][i] = __fadd_rn(v[h][i], r8[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss[h] = __fadd_rn(ss[h], __fmul_rn(v[h][i], v[h][i]));
+      }
+      const float total = row_sum_256(ss[0], ss[1], sh->red);
+      const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)kHidden), kEpsilon));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = h * 1024 + pt * 8;
+        const uint4 xs = pack8(v[h]);
+        if (res) __stcg(reinterpret_cast<uint4*>(x + (size_t)t * kHidden + c), xs);
+        float xn[8], o[8];
+        unpack8(xs, xn);
+        const float4 w0 = *reinterpret_cast<const float4*>(w + c);
+        const float4 w1 = *reinterpret_cast<const float4*>(w + c + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xn[i], inv), wv[i]);
+        __stcg(reinterpret_cast<uint4*>(out + (size_t)t * kHidden + c), pack8(o));
+      }
+    };
+
+    auto norm_phase = [&](__half* x, const __half* res, const float* w, __half* out, int T) {
+      for (int t = cta; t < T; t += G) norm_row(x, res, w, out, t);
+    };
+
+    // ---- embedding (ops.ts:680-725) + first RMSNorm, one token per item ----
+    for (int t = cta; t < T0; t += G) {
+      const int b = find_req(meta->src_off, batch, t);
+      const int p = t - meta->src_off[b];
+      uint32_t id = a.ids[(size_t)b * meta->seq + p];
+      if (id >= (uint32_t)a.vocab) id = 0;  // the host validates ids; keeps reads in bounds
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = h * 1024 + pt * 8;
+        const int within = c & 255, hf = within >> 7, position = within & 127;
+        const int quad = position >> 5, ln = position & 31;
+        const uint8_t* blk = a.embd + ((size_t)id * (kHidden / 256) + (c >> 8)) * 210;
+        const float d = half_at(blk + 208);
+        const int sc = (int)(int8_t)blk[192 + hf * 8 + ln / 16 + quad * 2];
+        const float ds = __fmul_rn(d, (float)sc);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int lb = blk[hf * 64 + ln + i + (quad & 1) * 32];
+          const int lo = quad >= 2 ? (lb >> 4) : (lb & 15);
+          const int hi = (blk[128 + hf * 32 + ln + i] >> (quad * 2)) & 3;
+          v[i] = __fmul_rn(ds, (float)((lo | (hi << 4)) - 32));
+        }
+        __stcg(reinterpret_cast<uint4*>(a.x + (size_t)t * kHidden + c), pack8(v));
+      }
+      norm_row(a.x, nullptr, a.attn_norm[0], a.nrm, t);
+    }
+    grid_barrier();
+
+    for (int l = 0; l < a.n_layers; ++l) {
+      const bool merged = l >= kMergeAfterLayer;
+      if (l == kMergeAfterLayer) {
+        // ---- token merge of x and the normalised state (ops.ts:629-661) ----
+        for (int t = cta; t < T1; t += G) {
+          const int b = find_req(meta->tgt_off, batch, t);
+          const uint32_t p = (uint32_t)(t - meta->tgt_off[b]);
+          const uint32_t sl = (uint32_t)meta->src_len[b], tl = (uint32_t)meta->tgt_len[b];
+          uint32_t start = 0, end = 1;
+          if (p > 0 && tl > 1) {
+            const uint32_t st = sl - 1, tt = tl - 1;
+            start = 1 + ((p - 1) * st) / tt;
+            end = 1 + (p * st) / tt;
+            end = max(end, start + 1);
+            end = min(end, sl);
+          }
+          const size_t src = (size_t)meta->src_off[b];
+          const float cnt = (float)(end - start);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = h * 1024 + pt * 8;
+            float tx[8] = {0, 0, 0, 0, 0, 0, 0, 0}, tn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (uint32_t s = start; s < end; ++s) {
+              float xv[8], nv[8];
+              unpack8(__ldcg(reinterpret_cast<const uint4*>(a.x + (src + s) * kHidden + c)), xv);
+              unpack8(__ldcg(reinterpret_cast<const uint4*>(a.nrm + (src + s) * kHidden + c)), nv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                tx[i] = __fadd_rn(tx[i], xv[i]);
+                tn[i] = __fadd_rn(tn[i], nv[i]);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              tx[i] = __fdiv_rn(tx[i], cnt);
+              tn[i] = __fdiv_rn(tn[i], cnt);
+            }
+            __stcg(reinterpret_cast<uint4*>(a.xm + (size_t)t * kHidden + c), pack8(tx));
+            __stcg(reinterpret_cast<uint4*>(a.nm + (size_t)t * kHidden + c), pack8(tn));
+          }
+        }
+        grid_barrier();
+      }
+      __half* X = merged ? a.xm : a.x;
+      __half* N = merged ? a.nm : a.nrm;
+      const int T = merged ? T1 : T0;
+
+      projection(l * 4 + 0, &a.xmap[merged ? 1 : 0], merged);
+      grid_barrier();
+
+      // ---- attention (ops.ts:295-362): one (request, q head) per item. Each
+      // warp scores its queries (4 dims per lane, butterfly sums) and keeps the
+      // softmax row in shared memory; then thread d accumulates dimension d of
+      // every query's output. ----
+      {
+        float* ks = reinterpret_cast<float*>(xring);  // [NP][128]
+        float* vs = ks + NP * kHeadDim;                // [NP][128]
+        float* qs = vs + NP * kHeadDim;                // [NP][128]
+        float* ps = qs + NP * kHeadDim;                // [NP][NP]
+        float* linv = ps + NP * NP;                    // [NP]
+        const int* off = merged ? meta->tgt_off : meta->src_off;
+        for (int item = cta; item < batch * kQHeads; item += G) {
+          const int b = item / kQHeads, h = item % kQHeads, kvh = h / (kQHeads / kKVHeads);
+          const int len = min(merged ? meta->tgt_len[b] : meta->src_len[b], NP);
+          const int base = off[b];
+          for (int i = pt; i < len * 16; i += 128) {
+            const int j = i >> 4, c = (i & 15) * 8;
+            float kv[8], vv[8], qv[8];
+            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.k + ((size_t)(base + j) * kKVHeads + kvh) * kHeadDim + c)), kv);
+            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.qkv + (size_t)(base + j) * kQKVWidth + kQWidth + kKVWidth +
+                                                          kvh * kHeadDim + c)),
+                    vv);
+            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.q + ((size_t)(base + j) * kQHeads + h) * kHeadDim + c)), qv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              ks[j * kHeadDim + c + e] = kv[e];
+              vs[j * kHeadDim + c + e] = vv[e];
+              qs[j * kHeadDim + c + e] = qv[e];
+            }
+          }
+          pw_sync();
+          const float scale = 0.08838834764831845f;
+          // scores: thread per (query, key) pair, four independent partial
+          // sums over dimensions (start staggered by key: no bank conflicts)
+          for (int e = pt; e < len * len; e += 128) {
+            const int i = e / len, j = e - i * len;
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+            for (int dd = 0; dd < kHeadDim; dd += 4) {
+              const int d = (dd + 4 * j) & (kHeadDim - 1);
+              const float4 q4 = *reinterpret_cast<const float4*>(qs + i * kHeadDim + d);
+              const float4 k4 = *reinterpret_cast<const float4*>(ks + j * kHeadDim + d);
+              s4[0] = fmaf(q4.x, k4.x, s4[0]);
+              s4[1] = fmaf(q4.y, k4.y, s4[1]);
+              s4[2] = fmaf(q4.z, k4.z, s4[2]);
+              s4[3] = fmaf(q4.w, k4.w, s4[3]);
+            }
+            const float temp = i >= 16384 ? logf(floorf((float)i / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
+            ps[i * NP + j] = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale * temp;
+          }
+          pw_sync();
+          if (pt < len) {  // softmax of query row pt
+            float m = -INFINITY;
+            for (int j = 0; j < len; ++j) m = fmaxf(m, ps[pt * NP + j]);
+            float l = 0.f;
+            for (int j = 0; j < len; ++j) {
+              const float p = expf(ps[pt * NP + j] - m);
+              ps[pt * NP + j] = p;
+              l += p;
+            }
+            linv[pt] = 1.0f / l;
+          }
+          pw_sync();
+          float acc[NP];
+#pragma unroll
+          for (int i = 0; i < NP; ++i) acc[i] = 0.f;
+          for (int j = 0; j < len; ++j) {
+            const float v = vs[j * kHeadDim + pt];
+#pragma unroll
+            for (int i = 0; i < NP; ++i) acc[i] = fmaf(ps[i * NP + j], v, acc[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < NP; ++i)
+            if (i < len) a.attn[(size_t)(base + i) * kQWidth + h * kHeadDim + pt] = __float2half_rn(acc[i] * linv[i]);
+          pw_sync();
+        }
+      }
+      grid_barrier();
+
+      projection(l * 4 + 1, &a.xmap[2], merged);
+      grid_barrier();
+      norm_phase(X, a.delta, a.ffn_norm[l], N, T);
+      grid_barrier();
+      projection(l * 4 + 2, &a.xmap[merged ? 1 : 0], merged);
+      grid_barrier();
+      projection(l * 4 + 3, &a.xmap[3], merged);
+      grid_barrier();
+      norm_phase(X, a.delta, l + 1 < a.n_layers ? a.attn_norm[l + 1] : a.output_norm, N, T);
+      grid_barrier();
+    }
+
+    // ---- mean pool over the valid merged rows + L2 (ops.ts:596-627) ----
+    for (int b = cta; b < batch; b += G) {
+      const int len = meta->tgt_len[b];
+      const size_t base = (size_t)meta->tgt_off[b];
+      float t[2][8];
+      float ss[2] = {0.f, 0.f};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = h * 1024 + pt * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[h][i] = 0.f;
+        for (int p = 0; p < len; ++p) {
+          float v[8];
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(a.nm + (base + p) * kHidden + c)), v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[h][i] = __fadd_rn(t[h][i], v[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          t[h][i] = __fdiv_rn(t[h][i], (float)len);
+          ss[h] = __fadd_rn(ss[h], __fmul_rn(t[h][i], t[h][i]));
+        }
+      }
+      const float inv = rsqrtf(row_sum_256(ss[0], ss[1], sh->red));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float4* o = reinterpret_cast<float4*>(a.out + (size_t)b * kHidden + h * 1024 + pt * 8);
+        o[0] = make_float4(t[h][0] * inv, t[h][1] * inv, t[h][2] * inv, t[h][3] * inv);
+        o[1] = make_float4(t[h][4] * inv, t[h][5] * inv, t[h][6] * inv, t[h][7] * inv);
+      }
+    }
+    // The last epilogue copy has landed before the CTA may exit.
+    if (pt == 0 && eph > 0) dev::mbar_wait(ebar, (eph - 1) & 1, err, 100000000ull);
+    // TMA loads of X issued without a matching MMA (after an error) land too.
+    if (pt == 0)
+      for (int j = xit > kXStages ? xit - kXStages : 0; j < xit; ++j)
+        dev::mbar_wait(xfull + 8 * (j % kXStages), (j / kXStages) & 1, err, 100000000ull);
+  }
+
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+size_t forward_smem_bytes(int chunk_max, int max_slots) {
+  constexpr int kXBytes = 4 * kFwdNP * 128;
+  return 1024 + (size_t)kXStages * kXBytes + (size_t)max_slots * kFwdNP * 128 * 4 +
+         (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6) +
+         sizeof(Shared);
+}
+
+cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
+  if (grid < 1 || a.max_slots < 1) return cudaErrorInvalidValue;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64) return cudaErrorInvalidValue;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(forward_kernel<kFwdNP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = forward_smem_bytes(a.chunk_max, a.max_slots);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barriers rely on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, forward_kernel<kFwdNP>, a);
+}
+
+cudaError_t forward_max_grid(int chunk_max, int max_slots, int* grid) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(forward_kernel<kFwdNP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<kFwdNP>, kThreads,
+                                                    forward_smem_bytes(chunk_max, max_slots));
+  if (e != cudaSuccess) return e;
+  // One CTA per SM: a second resident CTA could not allocate the full TMEM.
+  *grid = per_sm >= 1 ? sms : 0;
+  return cudaSuccess;
+}
+
+}  // namespace nemo

@@ -130,6 +130,56 @@ size_t skinny_smem_bytes(int np, int slabs_max, int chunk_max, int rstages);
 // np = tokens padded to 16, 32 or 64; map_x box 64 x np.
 cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np, int tiles, cudaStream_t s);
 
+// --- persistent single-launch forward for <= kFwdNP tokens (k_forward.cu) ---
+constexpr int kFwdNP = 16;        // token rows per projection (padded)
+constexpr int kFwdMaxTiles = 96;  // 128-row tiles of the widest projection (gate/up)
+
+struct FwdProj {
+  const uint8_t* packed;  // tile-slab image (see SkinnyTile)
+  const SkinnyTile* tiles;
+};
+
+// One CTA's share of one projection: a tile and a range of 256-column slabs.
+struct FwdSeg {
+  uint16_t proj;  // layer * 4 + projection (QKV, O, gate/up, down)
+  uint16_t tile;
+  uint8_t s0, s1;  // slabs [s0, s1)
+  uint8_t slot;    // partial-sum slot within the tile (slots follow K order)
+  uint8_t pad;
+};
+
+struct FwdArgs {
+  // Activation tensor maps, box 64 x kFwdNP, 128B swizzle: normalised state
+  // before / after the merge, attention output, SwiGLU output.
+  CUtensorMap xmap[4];
+  const FwdProj* proj;      // [n_layers * 4]
+  const FwdSeg* segs;       // per-CTA lists in forward order, concatenated
+  const int* seg_start;     // [grid + 1]
+  const uint8_t* nslots;    // [n_layers * 4][kFwdMaxTiles]
+  uint32_t* sync;           // [0] grid barrier, [1 + proj * kFwdMaxTiles + tile] tile counters; zero at launch
+  uint32_t* err;
+  const uint32_t* ids;      // [batch x seq]
+  const uint8_t* embd;
+  int vocab;
+  const float* attn_norm[kMaxLayers];
+  const float* ffn_norm[kMaxLayers];
+  const float* output_norm;
+  const Meta* meta;
+  const float* rope;
+  __half *x, *nrm, *xm, *nm, *qkv, *q, *k, *attn, *delta, *ffn;
+  float* part;              // [kFwdMaxTiles][max_slots][kFwdNP][128] f32, slots of a tile contiguous
+  int max_slots;
+  float* out;               // [batch x 2048]
+  int n_layers;
+  int chunk_max;
+};
+
+size_t forward_smem_bytes(int chunk_max, int max_slots);
+
+// Largest co-resident grid (one CTA per SM) or 0 if the kernel does not fit.
+cudaError_t forward_max_grid(int chunk_max, int max_slots, int* grid);
+cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s);
+
 // Host: encodes a 2-D f16 tensor map over a row-major [outer x inner] array
 // with a (box_inner x box_outer) box and 128-byte swizzle.
 int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

@@ -20,9 +20,10 @@ namespace nemo {
 int model_load(const void* data, size_t bytes, const int* devices, int ndev, nemo_model** out);
 void model_destroy(nemo_model* m);
 
-const char* kStageNames[11] = {"embedding_norm", "token_merge",  "qkv",         "rope_attention",
+const char* kStageNames[12] = {"embedding_norm", "token_merge",  "qkv",         "rope_attention",
                                "attention_output", "post_attention_norm", "ffn_up_gate", "swiglu",
-                               "ffn_down",         "post_ffn_norm",       "pool"};
+                               "ffn_down",         "post_ffn_norm",       "pool",        "forward_fused"};
+constexpr int kStageFused = 11;  // the whole forward as one persistent launch
 
 struct Profile {
   std::vector<cudaEvent_t> events;
@@ -85,6 +86,131 @@ int plan_alloc(DevicePlan& p, T** ptr, size_t bytes) {
   return kOk;
 }
 
+template <typename T>
+int plan_upload(DevicePlan& p, T** ptr, const std::vector<T>& host) {
+  if (int rc = plan_alloc(p, ptr, std::max<size_t>(host.size() * sizeof(T), 16))) return rc;
+  NEMO_CUDA_TRY(cudaMemcpy(*ptr, host.data(), host.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return kOk;
+}
+
+// Sets up the persistent single-launch forward when the plan's worst case fits
+// kFwdNP tokens (leaves p.fgrid = 0 otherwise). Weight work is split per
+// projection into grid-many contiguous ranges of the tile-major (tile, slab)
+// sequence; a range that crosses a tile boundary becomes two segments. Slots
+// of a tile are numbered in K order, so the partial sums of a tile are always
+// added in the same order. The CTA that takes range 0 rotates per projection
+// so the CTAs with one extra slab differ from projection to projection.
+int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
+  const int L = m->n_layers;
+  if (p.tmax0 > kFwdNP || L <= kMergeAfterLayer) return kOk;
+  const char* env = getenv("NEMO_FORWARD");
+  if (env && strcmp(env, "per_op") == 0) return kOk;
+  int chunk_max = 0;
+  for (int l = 0; l < L; ++l)
+    for (int w = 0; w < 4; ++w) {
+      const Projection& P = dm->proj[l][w];
+      if (P.tiles > kFwdMaxTiles || P.slabs > 255 || !P.packed) return kOk;
+      chunk_max = std::max(chunk_max, P.chunk_max);
+    }
+  int G = 0;
+  NEMO_CUDA_TRY(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, p.device));
+  if (G < 1) return kOk;
+
+  std::vector<std::vector<FwdSeg>> per(G);
+  std::vector<uint8_t> nslots((size_t)L * 4 * kFwdMaxTiles, 0);
+  int max_slots = 1;
+  for (int pi = 0; pi < L * 4; ++pi) {
+    const Projection& P = dm->proj[pi / 4][pi % 4];
+    const long long U = (long long)P.tiles * P.slabs;
+    const int rot = (int)(((long long)pi * 37) % G);
+    for (int ce = 0; ce < G; ++ce) {
+      const int u0 = (int)(ce * U / G), u1 = (int)((ce + 1) * U / G);
+      const int c = (ce + rot) % G;
+      for (int u = u0; u < u1;) {
+        const int tile = u / P.slabs, s0 = u % P.slabs;
+        const int s1 = std::min(P.slabs, s0 + (u1 - u));
+        uint8_t& n = nslots[(size_t)pi * kFwdMaxTiles + tile];
+        if (n == 255) return kOk;
+        FwdSeg sg;
+        sg.proj = (uint16_t)pi;
+        sg.tile = (uint16_t)tile;
+        sg.s0 = (uint8_t)s0;
+        sg.s1 = (uint8_t)s1;
+        sg.slot = n++;
+        sg.pad = 0;
+        max_slots = std::max(max_slots, (int)n);
+        per[c].push_back(sg);
+        u += s1 - s0;
+      }
+    }
+  }
+  std::vector<FwdSeg> segs;
+  std::vector<int> start(G + 1, 0);
+  for (int c = 0; c < G; ++c) {
+    start[c] = (int)segs.size();
+    segs.insert(segs.end(), per[c].begin(), per[c].end());
+  }
+  start[G] = (int)segs.size();
+  // The epilogue pulls all slots of a tile into shared memory at once.
+  if (forward_smem_bytes(chunk_max, max_slots) > 227 * 1024) return kOk;
+  int resident = 0;
+  NEMO_CUDA_TRY(forward_max_grid(chunk_max, max_slots, &resident));
+  if (resident != G) return kOk;
+  std::vector<FwdProj> proj((size_t)L * 4);
+  for (int pi = 0; pi < L * 4; ++pi) proj[pi] = {dm->proj[pi / 4][pi % 4].packed, dm->proj[pi / 4][pi % 4].d_tiles};
+
+  FwdArgs& a = p.fargs;
+  a = FwdArgs();
+  FwdProj* d_proj = nullptr;
+  FwdSeg* d_segs = nullptr;
+  int* d_start = nullptr;
+  uint8_t* d_nslots = nullptr;
+  if (plan_upload(p, &d_proj, proj) || plan_upload(p, &d_segs, segs) || plan_upload(p, &d_start, start) ||
+      plan_upload(p, &d_nslots, nslots))
+    return kErrCuda;
+  p.fsync_bytes = (size_t)(1 + L * 4 * kFwdMaxTiles) * 4;
+  if (plan_alloc(p, &p.fsync, p.fsync_bytes) ||
+      plan_alloc(p, &a.part, (size_t)kFwdMaxTiles * max_slots * kFwdNP * 128 * 4))
+    return kErrCuda;
+  a.proj = d_proj;
+  a.segs = d_segs;
+  a.seg_start = d_start;
+  a.nslots = d_nslots;
+  a.sync = p.fsync;
+  a.err = p.err;
+  a.ids = p.ids;
+  a.embd = dm->embd;
+  a.vocab = dm->vocab;
+  for (int l = 0; l < L; ++l) {
+    a.attn_norm[l] = dm->attn_norm[l];
+    a.ffn_norm[l] = dm->ffn_norm[l];
+  }
+  a.output_norm = dm->output_norm;
+  a.meta = p.meta;
+  a.rope = p.rope;
+  a.x = p.x;
+  a.nrm = p.norm;
+  a.xm = p.xm;
+  a.nm = p.nm;
+  a.qkv = p.qkv;
+  a.q = p.q;
+  a.k = p.k;
+  a.attn = p.attn;
+  a.delta = p.delta;
+  a.ffn = p.ffn;
+  a.max_slots = max_slots;
+  a.out = p.out;
+  a.n_layers = L;
+  a.chunk_max = chunk_max;
+  // X operands by TMA; the small-T maps (box 64 x 16) exist because tmax0 <= 16.
+  a.xmap[0] = p.xmap_norm[0];
+  a.xmap[1] = p.xmap_norm[1];
+  a.xmap[2] = p.xmap_attn[0];
+  a.xmap[3] = p.xmap_ffn[0];
+  p.fgrid = G;
+  return kOk;
+}
+
 void free_device_plan(DevicePlan& p) {
   cudaSetDevice(p.device);
   if (p.graph_host) cudaGraphExecDestroy(p.graph_host);
@@ -127,6 +253,13 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
   if (dump) {
     NEMO_CUDA_TRY(cudaMemcpyAsync(&host_meta, p.meta, sizeof(Meta), cudaMemcpyDeviceToHost, s));
     NEMO_CUDA_TRY(cudaStreamSynchronize(s));
+  }
+  if (p.fgrid && !dump) {
+    NEMO_CUDA_TRY(cudaMemsetAsync(p.fsync, 0, p.fsync_bytes, s));
+    stage(kStageFused);
+    NEMO_LAUNCH(launch_forward(p.fargs, p.fgrid, s));
+    stage(-1);
+    return kOk;
   }
   stage(0);
   NEMO_LAUNCH(launch_embedding(p.ids, dm.embd, dm.vocab, p.meta, p.tmax0, p.x, s));
@@ -352,6 +485,7 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, D
 
   // The lengths buffer must hold a valid run before the first launch.
   NEMO_CUDA_TRY(cudaMemcpy(p.lengths, p.h_lengths, (size_t)(cap_batch + 1) * 4, cudaMemcpyHostToDevice));
+  if (int rc = setup_forward(m, dm, p)) return rc;
   if (int rc = capture(p, m->n_layers, true, &p.graph_host)) return rc;
   if (int rc = capture(p, m->n_layers, false, &p.graph_device)) return rc;
   return kOk;
@@ -566,7 +700,7 @@ int plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint3
   int rc = enqueue_forward(p, plan->model->n_layers, p.stream, &prof, nullptr);
   NEMO_CUDA_TRY(cudaMemcpyAsync(p.h_err, p.err, 4, cudaMemcpyDeviceToHost, p.stream));
   NEMO_CUDA_TRY(cudaStreamSynchronize(p.stream));
-  for (int i = 0; i < 11; ++i) stage_ms[i] = 0.f;
+  for (int i = 0; i <= kStageFused; ++i) stage_ms[i] = 0.f;
   for (size_t i = 0; i + 1 < prof.events.size(); ++i) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, prof.events[i], prof.events[i + 1]);

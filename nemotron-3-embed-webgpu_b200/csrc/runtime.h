@@ -100,6 +100,13 @@ struct DevicePlan {
   bool gather[2] = {false, false};
   int splits[kMaxLayers][4] = {};
   int rstages[kMaxLayers][4] = {};
+  // Persistent single-launch forward (k_forward.cu) when the plan's worst case
+  // fits kFwdNP tokens: grid size (0 = per-op kernels), its arguments and the
+  // barrier / tile-counter block zeroed before each launch.
+  int fgrid = 0;
+  FwdArgs fargs = {};
+  uint32_t* fsync = nullptr;
+  size_t fsync_bytes = 0;
   cudaGraphExec_t graph_host = nullptr;    // H2D inputs -> forward -> D2H output
   cudaGraphExec_t graph_device = nullptr;  // forward only
   std::vector<void*> allocations;

@@ -20,7 +20,7 @@ import os
 import numpy as np
 
 HIDDEN = 2048
-NUM_STAGES = 11
+NUM_STAGES = 12
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "libnemo_b200.so")
 
@@ -58,6 +58,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_plan_run": (I, [P, P, S, P, S, P]),
         "nemo_plan_run_device": (I, [P, P, P, P]),
         "nemo_plan_stream": (P, [P]),
+        "nemo_plan_single_launch": (I, [P]),
         "nemo_plan_synchronize": (I, [P]),
         "nemo_plan_profile": (I, [P, P, S, P, S, P]),
         "nemo_stage_name": (ctypes.c_char_p, [I]),
@@ -141,6 +142,14 @@ class NemotronExecutionPlan:
 
     def stream(self) -> int:
         return load_library().nemo_plan_stream(self._h) or 0
+
+    @property
+    def fused(self) -> bool:
+        """True when the plan runs the forward as one persistent launch."""
+        r = load_library().nemo_plan_single_launch(self._h)
+        if r < 0:
+            check(r)
+        return r == 1
 
     def synchronize(self) -> None:
         check(load_library().nemo_plan_synchronize(self._h))
