@@ -69,6 +69,21 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// True in exactly one lane (the lowest) of the converged warp. Single-thread
+// async instructions (tcgen05.mma / commit, bulk and TMA copies) issue several
+// times faster from an elected lane of a converged warp than from a lone lane
+// whose siblings wait elsewhere; a tcgen05.commit must come from the same lane
+// as the MMAs it tracks, which elect.sync over a full warp guarantees (lane 0).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "elect.sync _|P1, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -136,6 +151,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(mbar)
                : "memory");
+}
+
+// L2 policy for data read once (streamed weights): evict first, so the small
+// activation and partial-sum buffers that phases exchange stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// bulk_load with an L2 cache-eviction policy.
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(mbar), "l"(policy)
+      : "memory");
 }
 
 // Makes this thread's generic-proxy shared-memory writes visible to the async

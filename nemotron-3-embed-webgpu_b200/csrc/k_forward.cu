@@ -80,6 +80,15 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 
 __device__ __forceinline__ void pw_sync() { dev::named_barrier(1, 128); }
 
+// 16-byte asynchronous global -> shared copy through L2 (many in flight per
+// thread without registers), and the wait for all of this thread's copies.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dev::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -126,6 +135,7 @@ __device__ __forceinline__ float row_sum_256(float s0, float s1, float* red) {
 struct Shared {
   uint32_t tmem;
   int flag;
+  int quiet;  // set while the phase warps run a latency-critical small phase
   float red[8];
 };
 
@@ -135,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   const uint32_t raw_s = dev::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
   constexpr int kXBytes = 4 * NP * 128;      // one 256-column slab of X: 4 x [NP rows x 64 f16]
-  constexpr int kSlotBytes = NP * 128 * 4;   // one partial-sum slot: [NP][128] f32
+  constexpr int kSlotBytes = NP * 128 * 4;   // slot-buffer unit: [NP][128] f32
   const int CM = a.chunk_max;
   // shared layout: X ring | epilogue slots | raw weight ring | barriers
   uint8_t* xring = smem;
@@ -147,11 +157,28 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   const uint32_t xfull = aempty + 8 * kASlabs, xempty = xfull + 8 * kXStages;
   const uint32_t dfull = xempty + 8 * kXStages, dempty = dfull + 16, fin = dempty + 16, ebar = fin + 8;
   Shared* sh = reinterpret_cast<Shared*>(bars + 2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6);
+  // Run metadata copied to shared memory once: this CTA's segments, slot
+  // counts and strides, the run's Meta and the RoPE rows of positions < NP.
+  FwdSeg* segs = reinterpret_cast<FwdSeg*>(reinterpret_cast<uint8_t*>(sh) + ((sizeof(Shared) + 15) & ~15));
+  Meta* meta = reinterpret_cast<Meta*>(segs + a.max_segs);
+  float* rope = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(meta + 1) + 15) & ~(uintptr_t)15);
+  int* sstride = reinterpret_cast<int*>(rope + NP * 128);
+  uint8_t* nslots = reinterpret_cast<uint8_t*>(sstride + a.n_layers * 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x, G = gridDim.x;
-  const FwdSeg* segs = a.segs + a.seg_start[cta];
-  const int nseg = a.seg_start[cta + 1] - a.seg_start[cta];
+  const int seg0 = a.seg_start[cta];
+  const int nseg = a.seg_start[cta + 1] - seg0;
   uint32_t* err = a.err;
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.segs + seg0);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(segs);
+    for (int i = threadIdx.x; i < nseg * (int)(sizeof(FwdSeg) / 4); i += kThreads) dst[i] = src[i];
+    for (int i = threadIdx.x; i < (int)(sizeof(Meta) / 4); i += kThreads)
+      reinterpret_cast<int*>(meta)[i] = reinterpret_cast<const int*>(a.meta)[i];
+    for (int i = threadIdx.x; i < NP * 128; i += kThreads) rope[i] = i < a.rope_rows * 128 ? a.rope[i] : 0.f;
+    for (int i = threadIdx.x; i < a.n_layers * 4; i += kThreads) sstride[i] = a.sstride[i];
+    for (int i = threadIdx.x; i < a.n_layers * 4 * kFwdMaxTiles; i += kThreads) nslots[i] = a.nslots[i];
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) dev::prefetch_tmap(&a.xmap[i]);
@@ -174,6 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     dev::mbar_init(fin, 1);
     dev::mbar_init(ebar, 1);
     dev::fence_mbar_init();
+    sh->flag = 0;
+    sh->quiet = 0;
   }
   if (warp == 1) {
     dev::tmem_alloc(dev::smem_u32(&sh->tmem), kTmemCols);
@@ -183,77 +212,87 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   __syncthreads();
   dev::tc_fence_after();
   const uint32_t tmem = sh->tmem;
-  // TMEM columns: two D buffers (segments alternate), each two accumulators
-  // (even / odd substages: independent MMA chains) of NP columns, then the A
-  // slabs.
-  const uint32_t tm_a = tmem + 4 * NP;
+  // TMEM columns: two D buffers (segments alternate), each four accumulators
+  // (one per 64-column substage: independent MMA chains) of NP columns, then
+  // the A slabs.
+  const uint32_t tm_a = tmem + 8 * NP;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int it = 0;
-      bool ok = true;
-      for (int si = 0; si < nseg && ok; ++si) {
-        const FwdSeg sg = segs[si];
-        const FwdProj P = a.proj[sg.proj];
-        const SkinnyTile ti = P.tiles[sg.tile];
-        const uint8_t* src = P.packed + ti.offset;
-        for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
-          const int s = it % kRawStages;
-          if (!wait(rempty + 8 * s, ((it / kRawStages) & 1) ^ 1, err)) {
-            ok = false;
-            break;
-          }
-          dev::mbar_arrive_expect_tx(rfull + 8 * s, ti.chunk_bytes);
-          dev::bulk_load(dev::smem_u32(raw + s * CM), src + (size_t)sl * ti.chunk_bytes, ti.chunk_bytes,
-                         rfull + 8 * s);
+    // The whole warp walks the schedule; one elected lane issues each copy.
+    // Weights are read once per forward: L2 evict-first keeps them from
+    // displacing the activations and partial sums the phases exchange.
+    const uint64_t policy = dev::l2_evict_first_policy();
+    int it = 0;
+    bool ok = true;
+    for (int si = 0; si < nseg && ok; ++si) {
+      const FwdSeg sg = segs[si];
+      for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
+        if (*reinterpret_cast<volatile int*>(&sh->quiet)) {
+          const uint64_t t0 = dev::globaltimer();
+          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < kLimitNs) __nanosleep(128);
         }
+        const int s = it % kRawStages;
+        if (!__all_sync(0xffffffffu, wait(rempty + 8 * s, ((it / kRawStages) & 1) ^ 1, err))) {
+          ok = false;
+          break;
+        }
+        if (dev::elect_one()) {
+          dev::mbar_arrive_expect_tx(rfull + 8 * s, sg.chunk_bytes);
+          dev::bulk_load_hint(dev::smem_u32(raw + s * CM), sg.chunk0 + (size_t)sl * sg.chunk_bytes, sg.chunk_bytes,
+                              rfull + 8 * s, policy);
+        }
+        __syncwarp();
       }
-      // Every issued copy lands before the CTA may exit.
-      for (int j = it > kRawStages ? it - kRawStages : 0; j < it; ++j)
-        dev::mbar_wait(rfull + 8 * (j % kRawStages), (j / kRawStages) & 1, err, 100000000ull);
     }
+    // Every issued copy lands before the CTA may exit.
+    for (int j = it > kRawStages ? it - kRawStages : 0; j < it; ++j)
+      dev::mbar_wait(rfull + 8 * (j % kRawStages), (j / kRawStages) & 1, err, 100000000ull);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
-      const uint32_t xbase = dev::smem_u32(xring);
-      int it = 0;
-      bool ok = true;
-      for (int si = 0; si < nseg && ok; ++si) {
-        const FwdSeg sg = segs[si];
-        const int d = si & 1;
-        if (!wait(dempty + 8 * d, ((si >> 1) & 1) ^ 1, err)) break;
+    // Converged warp, elected lane 0 issues every MMA and commit.
+    constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
+    const uint32_t xbase = dev::smem_u32(xring);
+    int it = 0;
+    bool ok = true;
+    for (int si = 0; si < nseg && ok; ++si) {
+      const FwdSeg sg = segs[si];
+      const int d = si & 1;
+      if (!__all_sync(0xffffffffu, wait(dempty + 8 * d, ((si >> 1) & 1) ^ 1, err))) break;
+      dev::tc_fence_after();
+      for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
+        const int xs = it % kXStages, s = it % kASlabs;
+        if (!__all_sync(0xffffffffu, wait(xfull + 8 * xs, (it / kXStages) & 1, err) &&
+                                         wait(afull + 8 * s, (it / kASlabs) & 1, err))) {
+          ok = false;
+          break;
+        }
         dev::tc_fence_after();
-        for (int sl = sg.s0; sl < sg.s1 && ok; ++sl, ++it) {
-          const int xs = it % kXStages;
-          if (!wait(xfull + 8 * xs, (it / kXStages) & 1, err)) {
-            ok = false;
-            break;
-          }
-          const int s = it % kASlabs;
-          if (!wait(afull + 8 * s, (it / kASlabs) & 1, err)) {
-            ok = false;
-            break;
-          }
-          dev::tc_fence_after();
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
+            if (dev::elect_one()) {
               const uint64_t bd = dev::make_sw128_desc(xbase + xs * kXBytes + q * NP * 128 + kk * 32);
-              dev::tc_mma_f16_ts(tmem + (2 * d + (q & 1)) * NP, tm_a + s * 128 + q * 32 + kk * 8, bd, idesc,
-                                 (sl != sg.s0 || q >= 2 || kk != 0) ? 1u : 0u);
+              dev::tc_mma_f16_ts(tmem + (4 * d + q) * NP, tm_a + s * 128 + q * 32 + kk * 8, bd, idesc,
+                                 (sl != sg.s0 || kk != 0) ? 1u : 0u);
             }
+            __syncwarp();
+          }
+        if (dev::elect_one()) {
           dev::tc_commit(aempty + 8 * s);
           dev::tc_commit(xempty + 8 * xs);
         }
-        if (ok) dev::tc_commit(dfull + 8 * d);
+        __syncwarp();
       }
-      // All issued MMAs complete before the TMEM is released.
-      dev::tc_commit(fin);
-      dev::mbar_wait(fin, 0, err, 100000000ull);
+      if (!ok) break;
+      if (dev::elect_one()) dev::tc_commit(dfull + 8 * d);
+      __syncwarp();
     }
+    // All issued MMAs complete before the TMEM is released.
+    if (dev::elect_one()) dev::tc_commit(fin);
+    __syncwarp();
+    dev::mbar_wait(fin, 0, err, 100000000ull);
   } else if (threadIdx.x < kPhaseThread0) {
     // ------------------------------------------------------------ decoders
     // Warp w writes TMEM lanes 32 * (w % 4) .. + 31, so its threads own those
@@ -267,10 +306,15 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     bool ok = true;
     for (int si = 0; si < nseg && ok; ++si) {
       const FwdSeg sg = segs[si];
-      const SkinnyTile ti = a.proj[sg.proj].tiles[sg.tile];
-      const int fmt = ti.fmt[half];
-      const int roff = half ? region_bytes(ti.fmt[0]) : 0;
+      const int fmt = sg.fmt[half];
+      const int roff = half ? region_bytes(sg.fmt[0]) : 0;
       for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
+        // Yield the SM's issue slots to the phase warps during small phases
+        // (attention, norms); bounded like every other wait.
+        if (*reinterpret_cast<volatile int*>(&sh->quiet)) {
+          const uint64_t t0 = dev::globaltimer();
+          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < kLimitNs) __nanosleep(128);
+        }
         const int rs = it % kRawStages;
         if (!__all_sync(0xffffffffu, wait(rfull + 8 * rs, (it / kRawStages) & 1, err))) {
           ok = false;
@@ -304,7 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     // ------------------------------------------------------------ phase warps
     const int pt = threadIdx.x - kPhaseThread0;
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const Meta* meta = a.meta;
     const int batch = min(meta->batch, kMaxBatch);
     const int T0 = min(meta->t0, NP), T1 = min(meta->t1, NP);
     int si = 0, xit = 0, gseg = 0, eph = 0;
@@ -336,55 +379,24 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       pw_sync();
     };
 
-    // Split-K epilogue of a finished tile: one bulk copy brings all of its
-    // partial slots (written by other CTAs, released through the tile counter)
-    // into shared memory; they are summed in slot (= K) order.
-    auto epilogue = [&](int pi, int tile, int T, bool merged) {
-      const int S = a.nslots[pi * kFwdMaxTiles + tile];
-      if (pt == 0) {
-        dev::fence_proxy_async_global();
-        dev::mbar_arrive_expect_tx(ebar, (uint32_t)(S * kSlotBytes));
-        dev::bulk_load(dev::smem_u32(ebuf), a.part + (size_t)tile * a.max_slots * (kSlotBytes / 4),
-                       (uint32_t)(S * kSlotBytes), ebar);
+    // Split-K epilogue of a finished gate/up tile: one bulk copy brings all of
+    // its partial slots (written by other CTAs, released through the tile
+    // counter) into shared memory; they are summed in slot (= K) order.
+    auto epilogue = [&](int pi, int tile, int T) {
+      const int S = nslots[pi * kFwdMaxTiles + tile], ss = sstride[pi];
+      if (pt < 32) {  // issued by lane 0 of the converged first phase warp
+        if (dev::elect_one()) {
+          dev::fence_proxy_async_global();
+          dev::mbar_arrive_expect_tx(ebar, (uint32_t)(T * ss * 512));
+          dev::bulk_load(dev::smem_u32(ebuf), a.part + (size_t)tile * NP * ss * 128, (uint32_t)(T * ss * 512), ebar);
+        }
+        __syncwarp();
       }
       const bool got = wait(ebar, eph & 1, err);
       ++eph;
-      const int which = pi & 3, n0 = tile * 128;
       // Each thread keeps one accumulator per token (independent chains) and
-      // adds the slots in order.
-      if (got && which == 0) {  // QKV: the reference stores f16 QKV, then rotates Q and K (ops.ts:168-194)
-        const int r = 2 * (pt & 63), tb = (pt >> 6) * (NP / 2);
-        float e[NP / 2], o[NP / 2];
-#pragma unroll
-        for (int j = 0; j < NP / 2; ++j) e[j] = o[j] = 0.f;
-        for (int s = 0; s < S; ++s)
-#pragma unroll
-          for (int j = 0; j < NP / 2; ++j) {
-            const float2 v = *reinterpret_cast<const float2*>(ebuf + (s * NP + tb + j) * 128 + r);
-            e[j] = __fadd_rn(e[j], v.x);
-            o[j] = __fadd_rn(o[j], v.y);
-          }
-        const int col = n0 + r;
-        const int* off = merged ? meta->tgt_off : meta->src_off;
-#pragma unroll
-        for (int j = 0; j < NP / 2; ++j) {
-          const int t = tb + j;
-          if (t >= T) break;
-          const float even = __half2float(__float2half_rn(e[j])), odd = __half2float(__float2half_rn(o[j]));
-          if (col < kQWidth + kKVWidth) {
-            const int b = find_req(off, batch, t);
-            const int pos = t - off[b];
-            const float2 cs = *reinterpret_cast<const float2*>(a.rope + ((size_t)pos * 64 + ((col & 127) >> 1)) * 2);
-            const __half2 h = __halves2half2(__float2half_rn(__fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y))),
-                                             __float2half_rn(__fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x))));
-            if (col < kQWidth) *reinterpret_cast<__half2*>(a.q + (size_t)t * kQWidth + col) = h;
-            else *reinterpret_cast<__half2*>(a.k + (size_t)t * kKVWidth + col - kQWidth) = h;
-          } else {
-            *reinterpret_cast<__half2*>(a.qkv + (size_t)t * kQKVWidth + col) =
-                __halves2half2(__float2half_rn(even), __float2half_rn(odd));
-          }
-        }
-      } else if (got && which == 2) {  // gate/up: f16 gate and up, then SwiGLU (ops.ts:74-89)
+      // adds the slots in order; f16 gate and up, then SwiGLU (ops.ts:74-89).
+      if (got) {
         const int r = pt & 63, tb = (pt >> 6) * (NP / 2);
         float g[NP / 2], u[NP / 2];
 #pragma unroll
@@ -392,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         for (int s = 0; s < S; ++s)
 #pragma unroll
           for (int j = 0; j < NP / 2; ++j) {
-            const float* p = ebuf + (s * NP + tb + j) * 128;
+            const float* p = ebuf + ((tb + j) * ss + s) * 128;
             g[j] = __fadd_rn(g[j], p[r]);
             u[j] = __fadd_rn(u[j], p[64 + r]);
           }
@@ -404,44 +416,47 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
           const float silu = __fdiv_rn(gh, __fadd_rn(1.0f, expf(-gh)));
           a.ffn[(size_t)t * kInter + tile * 64 + r] = __float2half_rn(__fmul_rn(silu, uh));
         }
-      } else if (got) {  // O and down: f16 delta
-        float acc[NP];
-#pragma unroll
-        for (int t = 0; t < NP; ++t) acc[t] = 0.f;
-        for (int s = 0; s < S; ++s)
-#pragma unroll
-          for (int t = 0; t < NP; ++t) acc[t] = __fadd_rn(acc[t], ebuf[(s * NP + t) * 128 + pt]);
-#pragma unroll
-        for (int t = 0; t < NP; ++t)
-          if (t < T) a.delta[(size_t)t * kHidden + n0 + pt] = __float2half_rn(acc[t]);
       }
       dev::fence_proxy_async_smem();  // these reads of ebuf precede the next bulk write into it
       pw_sync();
     };
 
-    // TMEM -> partial slot; the CTA that completes the tile runs its epilogue.
-    auto drain = [&](const FwdSeg& sg, int T, bool merged) {
+    // TMEM -> partial slot. QKV, O and down partials are summed by the next
+    // phase after the grid barrier; gate/up tiles are counted, and the CTA
+    // that completes one runs its SwiGLU epilogue (returns true).
+    auto drain = [&](const FwdSeg& sg, int T, bool counted) -> bool {
       const int d = gseg & 1;
       const bool got = __all_sync(0xffffffffu, wait(dfull + 8 * d, (gseg >> 1) & 1, err));
       ++gseg;
-      float* slot = a.part + ((size_t)sg.tile * a.max_slots + sg.slot) * (kSlotBytes / 4);
+      const int ss = sstride[sg.proj];
+      // O / down: token-major [t][tile][slot] (a norm row reads one block);
+      // QKV / gate-up: tile-major [tile][t][slot] (an attention head or a
+      // gate/up epilogue reads one block per tile).
+      const bool token_major = (sg.proj & 1) != 0;
+      const size_t tstride = token_major ? (size_t)(kHidden / 128) * ss * 128 : (size_t)ss * 128;
+      float* slot = a.part + (token_major ? (size_t)sg.tile * ss : (size_t)sg.tile * NP * ss) * 128 + (size_t)sg.slot * 128;
       if (got) {
         dev::tc_fence_after();
         const int row = quarter * 32 + lane;
 #pragma unroll
         for (int c0 = 0; c0 < NP; c0 += 16) {
-          uint32_t v0[16], v1[16];
-          const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + 2 * d * NP + c0;
+          uint32_t v0[16], v1[16], v2[16], v3[16];
+          const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + 4 * d * NP + c0;
           dev::tmem_ld_32x32b_x16(base, v0);
           dev::tmem_ld_32x32b_x16(base + NP, v1);
+          dev::tmem_ld_32x32b_x16(base + 2 * NP, v2);
+          dev::tmem_ld_32x32b_x16(base + 3 * NP, v3);
           dev::tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < T) __stcg(slot + (c0 + j) * 128 + row, __uint_as_float(v0[j]) + __uint_as_float(v1[j]));
+            if (c0 + j < T)
+              __stcg(slot + (size_t)(c0 + j) * tstride + row, (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) +
+                                                      (__uint_as_float(v2[j]) + __uint_as_float(v3[j])));
         }
       }
       dev::tc_fence_before();
       dev::mbar_arrive(dempty + 8 * d);
+      if (!counted) return false;
       pw_sync();
       if (pt == 0) {
         int last = 0;
@@ -449,40 +464,65 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
           __threadfence();
           const int idx = sg.proj * kFwdMaxTiles + sg.tile;
           const uint32_t old = atomicAdd(&a.sync[1 + idx], 1u);
-          last = old + 1 == (uint32_t)a.nslots[idx];
+          last = old + 1 == (uint32_t)nslots[idx];
           if (last) __threadfence();
         }
         sh->flag = last;
       }
       pw_sync();
-      if (*reinterpret_cast<volatile int*>(&sh->flag)) epilogue(sg.proj, sg.tile, T, merged);
+      return *reinterpret_cast<volatile int*>(&sh->flag) != 0;
     };
 
-    // X slabs by TMA (thread 0), then drains of the finished segments.
+    // X slabs by TMA (first phase warp, elected lane 0: the lane that made the
+    // barrier's acquire visible to the async proxy), then drains of the
+    // finished segments.
     auto projection = [&](int pi, const CUtensorMap* xmap, bool merged) {
       const int T = merged ? T1 : T0;
       const int first = si;
       while (si < nseg && segs[si].proj == pi) ++si;
+      const bool counted = (pi & 3) == 2;
+      int last_tiles[4], nlast = 0;
+      auto publish = [&](int j) {
+        if (drain(segs[j], T, counted) && nlast < 4) last_tiles[nlast++] = segs[j].tile;
+      };
       for (int j = first; j < si; ++j) {
         const FwdSeg sg = segs[j];
-        if (pt == 0) {
+        if (pt < 32) {
           for (int sl = sg.s0; sl < sg.s1; ++sl, ++xit) {
             const int xs = xit % kXStages;
-            if (wait(xempty + 8 * xs, ((xit / kXStages) & 1) ^ 1, err)) {
+            if (__all_sync(0xffffffffu, wait(xempty + 8 * xs, ((xit / kXStages) & 1) ^ 1, err)) && dev::elect_one()) {
               dev::mbar_arrive_expect_tx(xfull + 8 * xs, kXBytes);
               for (int q = 0; q < 4; ++q)
                 dev::tma_load_2d(dev::smem_u32(xring + xs * kXBytes + q * NP * 128), xmap, sl * 256 + q * 64, 0,
                                  xfull + 8 * xs);
             }
+            __syncwarp();
           }
         }
-        if (j > first) drain(segs[j - 1], T, merged);
+        if (j > first) publish(j - 1);
       }
-      if (si > first) drain(segs[si - 1], T, merged);
+      if (si > first) publish(si - 1);
+      for (int e = 0; e < nlast; ++e) epilogue(pi, last_tiles[e], T);
     };
 
-    // residual add (optional) + RMSNorm of one row (ops.ts:21-72).
-    auto norm_row = [&](__half* x, const __half* res, const float* w, __half* out, int t) {
+    float* stage = reinterpret_cast<float*>(xring);  // X ring + slot buffers, idle outside projections
+
+    // Residual add of projection rpi's output (rpi < 0: none) + RMSNorm of
+    // one row (ops.ts:21-72). The row's partial slots of the 16 output tiles
+    // are staged first: stage[(tile * ss + slot) * 128 + column].
+    auto norm_row = [&](__half* x, int rpi, const float* w, __half* out, int t) {
+      const bool res = rpi >= 0;
+      const int sst = res ? sstride[rpi] : 0;
+      if (res) {
+        const uint8_t* ns = nslots + rpi * kFwdMaxTiles;
+        (void)ns;
+        const float* src = a.part + (size_t)t * (kHidden / 128) * sst * 128 + pt * 4;
+        float* dst = stage + pt * 4;
+        const int n = (kHidden / 128) * sst * 32;  // 16-byte chunks of the row's block
+        for (int k = pt; k < n; k += 128, src += 512, dst += 512) cp_async16(dst, src);
+        cp_async_wait_all();
+        pw_sync();
+      }
       float v[2][8];
       float ss[2] = {0.f, 0.f};
 #pragma unroll
@@ -490,10 +530,18 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         const int c = h * 1024 + pt * 8;
         unpack8(__ldcg(reinterpret_cast<const uint4*>(x + (size_t)t * kHidden + c)), v[h]);
         if (res) {
-          float r8[8];
-          unpack8(__ldcg(reinterpret_cast<const uint4*>(res + (size_t)t * kHidden + c)), r8);
+          const int tile = c >> 7, S = nslots[rpi * kFwdMaxTiles + tile];
+          const float* p = stage + tile * sst * 128 + (c & 127);
+          float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int sl = 0; sl < S; ++sl) {
+            const float4 u0 = *reinterpret_cast<const float4*>(p + sl * 128);
+            const float4 u1 = *reinterpret_cast<const float4*>(p + sl * 128 + 4);
+            const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[h][i] = __fadd_rn(v[h][i], r8[i]);
+            for (int i = 0; i < 8; ++i) r8[i] = __fadd_rn(r8[i], uu[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[h][i] = __fadd_rn(v[h][i], __half2float(__float2half_rn(r8[i])));
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) ss[h] = __fadd_rn(ss[h], __fmul_rn(v[h][i], v[h][i]));
@@ -516,8 +564,13 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       }
     };
 
-    auto norm_phase = [&](__half* x, const __half* res, const float* w, __half* out, int T) {
-      for (int t = cta; t < T; t += G) norm_row(x, res, w, out, t);
+    auto set_quiet = [&](bool on) {
+      if (pt == 0) *reinterpret_cast<volatile int*>(&sh->quiet) = on ? 1 : 0;
+    };
+    auto norm_phase = [&](__half* x, int rpi, const float* w, __half* out, int T) {
+      set_quiet(true);
+      for (int t = cta; t < T; t += G) norm_row(x, rpi, w, out, t);
+      set_quiet(false);
     };
 
     // ---- embedding (ops.ts:680-725) + first RMSNorm, one token per item ----
@@ -545,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         }
         __stcg(reinterpret_cast<uint4*>(a.x + (size_t)t * kHidden + c), pack8(v));
       }
-      norm_row(a.x, nullptr, a.attn_norm[0], a.nrm, t);
+      norm_row(a.x, -1, a.attn_norm[0], a.nrm, t);
     }
     grid_barrier();
 
@@ -610,26 +663,62 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         float* ps = qs + NP * kHeadDim;                // [NP][NP]
         float* linv = ps + NP * NP;                    // [NP]
         const int* off = merged ? meta->tgt_off : meta->src_off;
+        const int qkv_pi = l * 4;
+        set_quiet(true);
         for (int item = cta; item < batch * kQHeads; item += G) {
           const int b = item / kQHeads, h = item % kQHeads, kvh = h / (kQHeads / kKVHeads);
           const int len = min(merged ? meta->tgt_len[b] : meta->src_len[b], NP);
           const int base = off[b];
-          for (int i = pt; i < len * 16; i += 128) {
-            const int j = i >> 4, c = (i & 15) * 8;
-            float kv[8], vv[8], qv[8];
-            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.k + ((size_t)(base + j) * kKVHeads + kvh) * kHeadDim + c)), kv);
-            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.qkv + (size_t)(base + j) * kQKVWidth + kQWidth + kKVWidth +
-                                                          kvh * kHeadDim + c)),
-                    vv);
-            unpack8(__ldcg(reinterpret_cast<const uint4*>(a.q + ((size_t)(base + j) * kQHeads + h) * kHeadDim + c)), qv);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              ks[j * kHeadDim + c + e] = kv[e];
-              vs[j * kHeadDim + c + e] = vv[e];
-              qs[j * kHeadDim + c + e] = qv[e];
+          // Q (tile h), K (tile 24 + kvh) and V (tile 32 + kvh) of the
+          // request's rows from the QKV partial slots, staged into the slot
+          // buffers in as few rounds as fit: f16 QKV, then RoPE on Q and K
+          // (ops.ts:168-194; position = row within the request).
+          const uint8_t* ns = nslots + qkv_pi * kFwdMaxTiles;
+          const int tiles[3] = {h, kQHeads + kvh, kQHeads + kKVHeads + kvh};
+          const int ss = sstride[qkv_pi];
+          const int cap = a.max_slots * NP;  // 128-float rows of the slot buffers
+          for (int p0 = 0; p0 < 3;) {
+            int p1 = p0;
+            while (p1 < 3 && (p1 == p0 || (p1 + 1 - p0) * ss * len <= cap)) ++p1;
+            const int per = len * ss * 32;  // 16-byte chunks per part: the request's rows, all slots
+            for (int pp = p0; pp < p1; ++pp) {
+              const float* src = a.part + ((size_t)tiles[pp] * NP + base) * ss * 128 + pt * 4;
+              float* dst = ebuf + (pp - p0) * len * ss * 128 + pt * 4;
+              for (int k = pt; k < per; k += 128, src += 512, dst += 512) cp_async16(dst, src);
             }
+            cp_async_wait_all();
+            pw_sync();
+            for (int pp = p0; pp < p1; ++pp)
+            for (int u = pt; u < len * 16; u += 128) {
+              const int j = u >> 4, c = (u & 15) * 8;
+              const int S = ns[tiles[pp]];
+              float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              for (int sl = 0; sl < S; ++sl) {
+                const float* q8 = ebuf + (((pp - p0) * len + j) * ss + sl) * 128 + c;
+                const float4 u0 = *reinterpret_cast<const float4*>(q8);
+                const float4 u1 = *reinterpret_cast<const float4*>(q8 + 4);
+                const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v8[e] = __fadd_rn(v8[e], uu[e]);
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v8[e] = __half2float(__float2half_rn(v8[e]));
+              float* dst = (pp == 0 ? qs : pp == 1 ? ks : vs) + j * kHeadDim + c;
+              if (pp < 2) {
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                  const float2 cs = *reinterpret_cast<const float2*>(rope + (j * 64 + ((c + e) >> 1)) * 2);
+                  dst[e] = __half2float(__float2half_rn(__fsub_rn(__fmul_rn(v8[e], cs.x), __fmul_rn(v8[e + 1], cs.y))));
+                  dst[e + 1] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(v8[e], cs.y), __fmul_rn(v8[e + 1], cs.x))));
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dst[e] = v8[e];
+              }
+            }
+            pw_sync();  // the slot buffers are refilled by the next round
+            p0 = p1;
           }
-          pw_sync();
           const float scale = 0.08838834764831845f;
           // scores: thread per (query, key) pair, four independent partial
           // sums over dimensions (start staggered by key: no bank conflicts)
@@ -675,18 +764,19 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
             if (i < len) a.attn[(size_t)(base + i) * kQWidth + h * kHeadDim + pt] = __float2half_rn(acc[i] * linv[i]);
           pw_sync();
         }
+        set_quiet(false);
       }
       grid_barrier();
 
       projection(l * 4 + 1, &a.xmap[2], merged);
       grid_barrier();
-      norm_phase(X, a.delta, a.ffn_norm[l], N, T);
+      norm_phase(X, l * 4 + 1, a.ffn_norm[l], N, T);
       grid_barrier();
       projection(l * 4 + 2, &a.xmap[merged ? 1 : 0], merged);
       grid_barrier();
       projection(l * 4 + 3, &a.xmap[3], merged);
       grid_barrier();
-      norm_phase(X, a.delta, l + 1 < a.n_layers ? a.attn_norm[l + 1] : a.output_norm, N, T);
+      norm_phase(X, l * 4 + 3, l + 1 < a.n_layers ? a.attn_norm[l + 1] : a.output_norm, N, T);
       grid_barrier();
     }
 
@@ -739,11 +829,12 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
 
 }  // namespace
 
-size_t forward_smem_bytes(int chunk_max, int max_slots) {
+size_t forward_smem_bytes(int chunk_max, int max_slots, int max_segs, int n_layers) {
   constexpr int kXBytes = 4 * kFwdNP * 128;
   return 1024 + (size_t)kXStages * kXBytes + (size_t)max_slots * kFwdNP * 128 * 4 +
          (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6) +
-         sizeof(Shared);
+         ((sizeof(Shared) + 15) & ~15) + (size_t)max_segs * sizeof(FwdSeg) + sizeof(Meta) + 16 + kFwdNP * 128 * 4 +
+         (size_t)n_layers * 4 * (4 + kFwdMaxTiles);
 }
 
 cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
@@ -761,7 +852,7 @@ cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = forward_smem_bytes(a.chunk_max, a.max_slots);
+  cfg.dynamicSmemBytes = forward_smem_bytes(a.chunk_max, a.max_slots, a.max_segs, a.n_layers);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barriers rely on it
@@ -771,7 +862,7 @@ cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, forward_kernel<kFwdNP>, a);
 }
 
-cudaError_t forward_max_grid(int chunk_max, int max_slots, int* grid) {
+cudaError_t forward_max_grid(size_t smem_bytes, int* grid) {
   int dev = 0, sms = 0, per_sm = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -779,8 +870,7 @@ cudaError_t forward_max_grid(int chunk_max, int max_slots, int* grid) {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(forward_kernel<kFwdNP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<kFwdNP>, kThreads,
-                                                    forward_smem_bytes(chunk_max, max_slots));
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<kFwdNP>, kThreads, smem_bytes);
   if (e != cudaSuccess) return e;
   // One CTA per SM: a second resident CTA could not allocate the full TMEM.
   *grid = per_sm >= 1 ? sms : 0;

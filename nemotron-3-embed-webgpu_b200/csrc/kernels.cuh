@@ -134,25 +134,24 @@ cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np,
 constexpr int kFwdNP = 16;        // token rows per projection (padded)
 constexpr int kFwdMaxTiles = 96;  // 128-row tiles of the widest projection (gate/up)
 
-struct FwdProj {
-  const uint8_t* packed;  // tile-slab image (see SkinnyTile)
-  const SkinnyTile* tiles;
-};
-
-// One CTA's share of one projection: a tile and a range of 256-column slabs.
+// One CTA's share of one projection: a tile and a range of 256-column slabs,
+// with the tile's location in the projection's tile-slab image.
 struct FwdSeg {
-  uint16_t proj;  // layer * 4 + projection (QKV, O, gate/up, down)
+  const uint8_t* chunk0;  // chunk (tile, slab 0); slab s at chunk0 + s * chunk_bytes
+  uint32_t chunk_bytes;
+  uint16_t proj;          // layer * 4 + projection (QKV, O, gate/up, down)
   uint16_t tile;
-  uint8_t s0, s1;  // slabs [s0, s1)
-  uint8_t slot;    // partial-sum slot within the tile (slots follow K order)
-  uint8_t pad;
+  uint8_t s0, s1;         // slabs [s0, s1)
+  uint8_t slot;           // partial-sum slot within the tile (slots follow K order)
+  uint8_t fmt[2];         // SegFormat of the tile's two 64-row regions
+  uint8_t pad[3];
 };
 
 struct FwdArgs {
   // Activation tensor maps, box 64 x kFwdNP, 128B swizzle: normalised state
   // before / after the merge, attention output, SwiGLU output.
   CUtensorMap xmap[4];
-  const FwdProj* proj;      // [n_layers * 4]
+  const int* sstride;       // [n_layers * 4] partial-slot stride (largest slot count of the projection's tiles)
   const FwdSeg* segs;       // per-CTA lists in forward order, concatenated
   const int* seg_start;     // [grid + 1]
   const uint8_t* nslots;    // [n_layers * 4][kFwdMaxTiles]
@@ -166,18 +165,20 @@ struct FwdArgs {
   const float* output_norm;
   const Meta* meta;
   const float* rope;
+  int rope_rows;            // positions in the RoPE table (the plan's sequence, <= kFwdNP here)
   __half *x, *nrm, *xm, *nm, *qkv, *q, *k, *attn, *delta, *ffn;
-  float* part;              // [kFwdMaxTiles][max_slots][kFwdNP][128] f32, slots of a tile contiguous
+  float* part;              // [tile][kFwdNP tokens][sstride slots][128] f32 per projection
   int max_slots;
+  int max_segs;             // most segments any CTA owns
   float* out;               // [batch x 2048]
   int n_layers;
   int chunk_max;
 };
 
-size_t forward_smem_bytes(int chunk_max, int max_slots);
+size_t forward_smem_bytes(int chunk_max, int max_slots, int max_segs, int n_layers);
 
 // Largest co-resident grid (one CTA per SM) or 0 if the kernel does not fit.
-cudaError_t forward_max_grid(int chunk_max, int max_slots, int* grid);
+cudaError_t forward_max_grid(size_t smem_bytes, int* grid);
 cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s);
 
 // Host: encodes a 2-D f16 tensor map over a row-major [outer x inner] array

@@ -119,25 +119,33 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   std::vector<std::vector<FwdSeg>> per(G);
   std::vector<uint8_t> nslots((size_t)L * 4 * kFwdMaxTiles, 0);
   int max_slots = 1;
+  std::vector<SkinnyTile> tiles;
   for (int pi = 0; pi < L * 4; ++pi) {
     const Projection& P = dm->proj[pi / 4][pi % 4];
+    tiles.resize(P.tiles);
+    NEMO_CUDA_TRY(cudaMemcpy(tiles.data(), P.d_tiles, P.tiles * sizeof(SkinnyTile), cudaMemcpyDeviceToHost));
     const long long U = (long long)P.tiles * P.slabs;
     const int rot = (int)(((long long)pi * 37) % G);
     for (int ce = 0; ce < G; ++ce) {
       const int u0 = (int)(ce * U / G), u1 = (int)((ce + 1) * U / G);
       const int c = (ce + rot) % G;
+      // a CTA runs the epilogues of at most 4 tiles per projection
+      if (u1 > u0 && (u1 - 1) / P.slabs - u0 / P.slabs + 1 > 4) return kOk;
       for (int u = u0; u < u1;) {
         const int tile = u / P.slabs, s0 = u % P.slabs;
         const int s1 = std::min(P.slabs, s0 + (u1 - u));
         uint8_t& n = nslots[(size_t)pi * kFwdMaxTiles + tile];
         if (n == 255) return kOk;
-        FwdSeg sg;
+        FwdSeg sg = {};
+        sg.chunk0 = P.packed + tiles[tile].offset;
+        sg.chunk_bytes = tiles[tile].chunk_bytes;
         sg.proj = (uint16_t)pi;
         sg.tile = (uint16_t)tile;
         sg.s0 = (uint8_t)s0;
         sg.s1 = (uint8_t)s1;
         sg.slot = n++;
-        sg.pad = 0;
+        sg.fmt[0] = tiles[tile].fmt[0];
+        sg.fmt[1] = tiles[tile].fmt[1];
         max_slots = std::max(max_slots, (int)n);
         per[c].push_back(sg);
         u += s1 - s0;
@@ -146,33 +154,37 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   }
   std::vector<FwdSeg> segs;
   std::vector<int> start(G + 1, 0);
+  int max_segs = 1;
   for (int c = 0; c < G; ++c) {
     start[c] = (int)segs.size();
     segs.insert(segs.end(), per[c].begin(), per[c].end());
+    max_segs = std::max(max_segs, (int)per[c].size());
   }
   start[G] = (int)segs.size();
   // The epilogue pulls all slots of a tile into shared memory at once.
-  if (forward_smem_bytes(chunk_max, max_slots) > 227 * 1024) return kOk;
+  const size_t smem = forward_smem_bytes(chunk_max, max_slots, max_segs, L);
+  if (smem > 227 * 1024) return kOk;
   int resident = 0;
-  NEMO_CUDA_TRY(forward_max_grid(chunk_max, max_slots, &resident));
+  NEMO_CUDA_TRY(forward_max_grid(smem, &resident));
   if (resident != G) return kOk;
-  std::vector<FwdProj> proj((size_t)L * 4);
-  for (int pi = 0; pi < L * 4; ++pi) proj[pi] = {dm->proj[pi / 4][pi % 4].packed, dm->proj[pi / 4][pi % 4].d_tiles};
+  std::vector<int> sstride((size_t)L * 4, 1);
+  for (int pi = 0; pi < L * 4; ++pi)
+    for (int t = 0; t < kFwdMaxTiles; ++t) sstride[pi] = std::max(sstride[pi], (int)nslots[(size_t)pi * kFwdMaxTiles + t]);
 
   FwdArgs& a = p.fargs;
   a = FwdArgs();
-  FwdProj* d_proj = nullptr;
+  int* d_sstride = nullptr;
   FwdSeg* d_segs = nullptr;
   int* d_start = nullptr;
   uint8_t* d_nslots = nullptr;
-  if (plan_upload(p, &d_proj, proj) || plan_upload(p, &d_segs, segs) || plan_upload(p, &d_start, start) ||
+  if (plan_upload(p, &d_sstride, sstride) || plan_upload(p, &d_segs, segs) || plan_upload(p, &d_start, start) ||
       plan_upload(p, &d_nslots, nslots))
     return kErrCuda;
   p.fsync_bytes = (size_t)(1 + L * 4 * kFwdMaxTiles) * 4;
   if (plan_alloc(p, &p.fsync, p.fsync_bytes) ||
       plan_alloc(p, &a.part, (size_t)kFwdMaxTiles * max_slots * kFwdNP * 128 * 4))
     return kErrCuda;
-  a.proj = d_proj;
+  a.sstride = d_sstride;
   a.segs = d_segs;
   a.seg_start = d_start;
   a.nslots = d_nslots;
@@ -199,6 +211,8 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   a.delta = p.delta;
   a.ffn = p.ffn;
   a.max_slots = max_slots;
+  a.max_segs = max_segs;
+  a.rope_rows = p.seq;
   a.out = p.out;
   a.n_layers = L;
   a.chunk_max = chunk_max;

@@ -76,8 +76,11 @@ __device__ __forceinline__ int region_bytes(int fmt) { return fmt == kSegQ6K ? 6
 
 // Q4_K row block (GGUF 144 B). Quarter q = elements 64q..64q+63 of the slab.
 // value = f32(d*sc*q - dmin*m) (quantization.ts:33-34): s = d*sc and
-// o = dmin*m are exact; fma(s, 2^23+q, -s*2^23) = s*q exactly; one rounding
-// in the subtraction of o, as in the reference.
+// o = dmin*m are exact; one rounding in the subtraction of o, as in the
+// reference. A nibble at bit p of a word is masked in place under the f32
+// exponent of 2^23: (w & (15 << p)) | 0x4B000000 = 2^23 + q * 2^p (p <= 12
+// here), and fma(s * 2^-p, 2^23 + q * 2^p, -s * 2^(23-p)) = s * q exactly
+// (s * 2^-p is exact: s >= 2^-24 stays far above the f32 subnormal range).
 template <typename Sink>
 __device__ __forceinline__ void decode_q4k(const uint8_t* blk, int q, Sink&& sink) {
   const float d = half_at(blk), dmin = half_at(blk + 2);
@@ -97,24 +100,25 @@ __device__ __forceinline__ void decode_q4k(const uint8_t* blk, int q, Sink&& sin
   }
   const float s_lo = __fmul_rn(d, (float)sc_lo), s_hi = __fmul_rn(d, (float)sc_hi);
   const float o_lo = __fmul_rn(dmin, (float)m_lo), o_hi = __fmul_rn(dmin, (float)m_hi);
-  const float c_lo = -__fmul_rn(s_lo, 8388608.0f), c_hi = -__fmul_rn(s_hi, 8388608.0f);
-  const uint64_t S_lo = f2(s_lo, s_lo), S_hi = f2(s_hi, s_hi);
-  const uint64_t C_lo = f2(c_lo, c_lo), C_hi = f2(c_hi, c_hi);
+  // low nibbles at bits 0 and 8, high nibbles at bits 4 and 12 (of w or w >> 16)
+  const uint64_t S_lo = f2(s_lo, __fmul_rn(s_lo, 0x1p-8f)), S_hi = f2(__fmul_rn(s_hi, 0x1p-4f), __fmul_rn(s_hi, 0x1p-12f));
+  const uint64_t C_lo = f2(-__fmul_rn(s_lo, 0x1p23f), -__fmul_rn(s_lo, 0x1p15f));
+  const uint64_t C_hi = f2(-__fmul_rn(s_hi, 0x1p19f), -__fmul_rn(s_hi, 0x1p11f));
   const uint64_t O_lo = f2(-o_lo, -o_lo), O_hi = f2(-o_hi, -o_hi);
   const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + q * 32);
   const uint4 w0 = qv[0], w1 = qv[1];
   const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const int sh = c < 4 ? 0 : 4;
+    const uint32_t m0 = c < 4 ? 0x0Fu : 0xF0u, m1 = m0 << 8;
     const uint64_t S = c < 4 ? S_lo : S_hi, C = c < 4 ? C_lo : C_hi, O = c < 4 ? O_lo : O_hi;
     const uint32_t wa = w[(c & 3) * 2], wb = w[(c & 3) * 2 + 1];
     uint32_t h[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t src = i < 2 ? wa : wb;
-      const int b0 = (i & 1) * 2;
-      const uint64_t qf = f2(magic((src >> (8 * b0 + sh)) & 15u), magic((src >> (8 * b0 + 8 + sh)) & 15u));
+      const uint32_t x = (i & 1) ? src >> 16 : src;
+      const uint64_t qf = f2(__uint_as_float((x & m0) | 0x4B000000u), __uint_as_float((x & m1) | 0x4B000000u));
       h[i] = f2_to_h2(fadd2(ffma2(S, qf, C), O));
     }
     sink(c, make_uint4(h[0], h[1], h[2], h[3]));
