@@ -70,6 +70,12 @@ def kernels_per_forward(n_layers: int, fused: bool, max_tokens: int) -> int:
     return 3 + per_layer * n_layers + 2
 
 
+# DRAM bytes (read + write) per launch of the single-launch forward, from one
+# ncu capture of that kernel on this workload (dram__bytes.sum.per_second x
+# gpu__time_duration.sum); null where no capture was taken.
+NCU_TRAFFIC = {("config2", "kquant"): 534.2e6}
+
+
 def measured_peaks() -> dict:
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -299,7 +305,7 @@ def run_ours(args) -> None:
         achieved = flops / (gemm_ms / 1e3) / 1e12
         peak = peaks["bf16_tflops"]
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                "traffic": None, "kernel": kernel,
+                "traffic": NCU_TRAFFIC.get((args.workload, args.pack)) if fused else None, "kernel": kernel,
                 "kernel_ms_per_forward": gemm_ms, "algorithmic_per_forward": work,
                 "peak_source": peaks["source"], "stage_ms": prof}
 

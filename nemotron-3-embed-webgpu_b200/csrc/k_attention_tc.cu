@@ -15,7 +15,7 @@
 //               (double-buffered ring); V comes straight out of the QKV
 //               projection buffer and is consumed MN-major
 //   warp 1      TMEM allocation (512 columns: S ping-pong 2 x 128, O 128) and
-//               single-thread tcgen05.mma issue: S_j = Q.K_j^T, O += P_j.V_j
+//               tcgen05.mma issue (elected lane): S_j = Q.K_j^T, O += P_j.V_j
 //   warps 2..5  softmax (thread = query row): tcgen05.ld of the S row, online
 //               max/sum, P_j (f16) into 128B-swizzled shared memory, O row
 //               rescaled in TMEM (tcgen05.ld/st) when the running max moves;
@@ -115,70 +115,85 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      dev::pdl_wait();
+    // Converged warp; the elected lane issues the copies.
+    dev::pdl_wait();
+    if (dev::elect_one()) {
       dev::mbar_arrive_expect_tx(q_full, kTileBytes);
       dev::tma_load_2d(dev::smem_u32(sQ), &map_q, h * kHeadDim, base + q0, q_full);
       dev::tma_load_2d(dev::smem_u32(sQ + kHalfTile), &map_q, h * kHeadDim + 64, base + q0, q_full);
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j & 1;
-        if (!dev::mbar_wait(kv_empty + 8 * st, ((j >> 1) & 1) ^ 1, a.err)) break;
-        const uint32_t fb = kv_full + 8 * st;
+    }
+    __syncwarp();
+    int issued = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_empty + 8 * st, ((j >> 1) & 1) ^ 1, a.err))) break;
+      const uint32_t fb = kv_full + 8 * st;
+      const uint32_t dk = dev::smem_u32(sK + st * kTileBytes), dv = dev::smem_u32(sV + st * kTileBytes);
+      const int row = kbase + j * kTile;
+      if (dev::elect_one()) {
         dev::mbar_arrive_expect_tx(fb, 2 * kTileBytes);
-        const uint32_t dk = dev::smem_u32(sK + st * kTileBytes), dv = dev::smem_u32(sV + st * kTileBytes);
-        const int row = kbase + j * kTile;
         dev::tma_load_2d(dk, km, kcol, row, fb);
         dev::tma_load_2d(dk + kHalfTile, km, kcol + 64, row, fb);
         dev::tma_load_2d(dv, vm, vcol, row, fb);
         dev::tma_load_2d(dv + kHalfTile, vm, vcol + 64, row, fb);
-        ++issued;
       }
-      dev::mbar_wait(q_full, 0, a.err, 100000000ull);
-      for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
-        dev::mbar_wait(kv_full + 8 * (i & 1), (i >> 1) & 1, a.err, 100000000ull);
+      __syncwarp();
+      ++issued;
     }
+    dev::mbar_wait(q_full, 0, a.err, 100000000ull);
+    for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
+      dev::mbar_wait(kv_full + 8 * (i & 1), (i >> 1) & 1, a.err, 100000000ull);
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc_s = dev::make_idesc_f16(kTile, kTile);             // Q.K^T, both K-major
-      const uint32_t idesc_o = dev::make_idesc_f16(kTile, kHeadDim) | (1u << 16);  // P.V, V MN-major
-      const uint32_t aq = dev::smem_u32(sQ), ap = dev::smem_u32(sP);
-      bool ok = dev::mbar_wait(q_full, 0, a.err);
-      auto pv = [&](int i) -> bool {
-        if (!dev::mbar_wait(p_ready, i & 1, a.err)) return false;
-        dev::tc_fence_after();
-        const uint32_t bv = dev::smem_u32(sV + (i & 1) * kTileBytes);
+    // Converged warp; the elected lane (lane 0) issues every MMA and commit.
+    const uint32_t idesc_s = dev::make_idesc_f16(kTile, kTile);             // Q.K^T, both K-major
+    const uint32_t idesc_o = dev::make_idesc_f16(kTile, kHeadDim) | (1u << 16);  // P.V, V MN-major
+    const uint32_t aq = dev::smem_u32(sQ), ap = dev::smem_u32(sP);
+    bool ok = __all_sync(0xffffffffu, dev::mbar_wait(q_full, 0, a.err));
+    auto pv = [&](int i) -> bool {
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(p_ready, i & 1, a.err))) return false;
+      dev::tc_fence_after();
+      const uint32_t bv = dev::smem_u32(sV + (i & 1) * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
+      for (int kk = 0; kk < kTile / 16; ++kk) {
+        if (dev::elect_one()) {
           const uint64_t ad = dev::make_sw128_desc(ap + (kk >> 2) * kHalfTile + (kk & 3) * 32);
           const uint64_t bd = dev::make_sw128_desc_mn(bv + kk * 2048, kHalfTile, 1024);
           dev::tc_mma_f16(tmem + kColO, ad, bd, idesc_o, (i | kk) != 0 ? 1u : 0u);
         }
+        __syncwarp();
+      }
+      if (dev::elect_one()) {
         dev::tc_commit(pv_done);
         dev::tc_commit(kv_empty + 8 * (i & 1));
-        return true;
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j & 1;
-        if (!dev::mbar_wait(kv_full + 8 * st, (j >> 1) & 1, a.err)) {
-          ok = false;
-          break;
-        }
-        dev::tc_fence_after();
-        const uint32_t bk = dev::smem_u32(sK + st * kTileBytes);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full + 8 * st, (j >> 1) & 1, a.err))) {
+        ok = false;
+        break;
+      }
+      dev::tc_fence_after();
+      const uint32_t bk = dev::smem_u32(sK + st * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+      for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+        if (dev::elect_one()) {
           const uint64_t ad = dev::make_sw128_desc(aq + (kk >> 2) * kHalfTile + (kk & 3) * 32);
           const uint64_t bd = dev::make_sw128_desc(bk + (kk >> 2) * kHalfTile + (kk & 3) * 32);
           dev::tc_mma_f16(tmem + kColS + st * kTile, ad, bd, idesc_s, kk != 0 ? 1u : 0u);
         }
-        dev::tc_commit(s_full + 8 * st);
-        if (j >= 1) ok = pv(j - 1);
+        __syncwarp();
       }
-      if (ok) pv(ntiles - 1);
-      dev::tc_commit(mma_fin);
-      dev::mbar_wait(mma_fin, 0, a.err, 100000000ull);  // every MMA retired before TMEM is freed
+      if (dev::elect_one()) dev::tc_commit(s_full + 8 * st);
+      __syncwarp();
+      if (j >= 1) ok = pv(j - 1);
     }
+    if (ok) pv(ntiles - 1);
+    if (dev::elect_one()) dev::tc_commit(mma_fin);
+    __syncwarp();
+    dev::mbar_wait(mma_fin, 0, a.err, 100000000ull);  // every MMA retired before TMEM is freed
   } else {
     // ---- softmax warps: thread = query row (TMEM lane) ----
     const int quarter = warp & 3;

@@ -8,8 +8,9 @@
 // One CTA computes a 128 x BN tile. Warp roles (192 threads):
 //   warp 0      TMA producer: 64-wide K slabs of A (128 x 64) and B (BN x 64)
 //               into a STAGES-deep ring, 128-byte swizzled, mbarrier complete_tx
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128,
-//               N=BN, K=16 per instruction), tcgen05.commit frees each stage
+//   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16 per
+//               instruction; converged warp, elected lane), tcgen05.commit
+//               frees each stage
 //   warps 2..5  epilogue: tcgen05.ld 32x32b (one row per thread), f16 store
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error word,
 // drains what this CTA has in flight and frees its TMEM before returning.
@@ -75,43 +76,49 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % C::STAGES;
-        const uint32_t ph = (kt / C::STAGES) & 1;
-        if (!dev::mbar_wait(empty0 + 8 * s, ph ^ 1, err)) break;
-        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+    // Converged warp; the elected lane issues the copies.
+    int issued = 0;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % C::STAGES;
+      const uint32_t ph = (kt / C::STAGES) & 1;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(empty0 + 8 * s, ph ^ 1, err))) break;
+      const uint32_t sa = sbase + s * C::STAGE_BYTES;
+      if (dev::elect_one()) {
         dev::mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES);
         dev::tma_load_2d(sa, &map_a, kt * C::BK, m0, full0 + 8 * s);
         dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
-        ++issued;
       }
-      // Drain: every issued copy has landed before shared memory is released.
-      for (int i = issued > C::STAGES ? issued - C::STAGES : 0; i < issued; ++i)
-        dev::mbar_wait(full0 + 8 * (i % C::STAGES), (i / C::STAGES) & 1, err, 100000000ull);
+      __syncwarp();
+      ++issued;
     }
+    // Drain: every issued copy has landed before shared memory is released.
+    for (int i = issued > C::STAGES ? issued - C::STAGES : 0; i < issued; ++i)
+      dev::mbar_wait(full0 + 8 * (i % C::STAGES), (i / C::STAGES) & 1, err, 100000000ull);
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = dev::make_idesc_f16(C::BM, BN);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % C::STAGES;
-        const uint32_t ph = (kt / C::STAGES) & 1;
-        if (!dev::mbar_wait(full0 + 8 * s, ph, err)) break;
-        dev::tc_fence_after();
-        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+    // Converged warp; the elected lane (lane 0) issues every MMA and commit.
+    constexpr uint32_t idesc = dev::make_idesc_f16(C::BM, BN);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % C::STAGES;
+      const uint32_t ph = (kt / C::STAGES) & 1;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(full0 + 8 * s, ph, err))) break;
+      dev::tc_fence_after();
+      const uint32_t sa = sbase + s * C::STAGE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < C::BK / 16; ++kk) {
+      for (int kk = 0; kk < C::BK / 16; ++kk) {
+        if (dev::elect_one()) {
           const uint64_t ad = dev::make_sw128_desc(sa + kk * 32);
           const uint64_t bd = dev::make_sw128_desc(sa + C::A_BYTES + kk * 32);
           dev::tc_mma_f16(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
         }
-        dev::tc_commit(empty0 + 8 * s);
+        __syncwarp();
       }
-      dev::tc_commit(accum);
-      // All MMAs of this CTA have retired before TMEM is released below.
-      dev::mbar_wait(accum, 0, err, 100000000ull);
+      if (dev::elect_one()) dev::tc_commit(empty0 + 8 * s);
+      __syncwarp();
     }
+    if (dev::elect_one()) dev::tc_commit(accum);
+    __syncwarp();
+    // All MMAs of this CTA have retired before TMEM is released below.
+    dev::mbar_wait(accum, 0, err, 100000000ull);
   } else {
     const int quarter = warp & 3;
     const int row = m0 + quarter * 32 + lane;

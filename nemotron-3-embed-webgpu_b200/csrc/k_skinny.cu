@@ -11,7 +11,7 @@
 //               128-row x 256-column chunk per ring stage, cp.async.bulk)
 //               before waiting on the previous kernel, then TMA-loads the
 //               activation K range (box 64 x NP, 128B swizzle)
-//   warp 1      TMEM allocation + single-thread tcgen05.mma issue
+//   warp 1      TMEM allocation + tcgen05.mma issue (elected lane)
 //   warps 2..5  decoders (thread = weight row): exact decode of the block
 //               with the reference's arithmetic (quantization.ts:19-74; every
 //               intermediate is exact or rounded once, as there), f16 round to
@@ -87,60 +87,72 @@ __global__ void __launch_bounds__(192, 1)
   const uint8_t* chunk0 = a.packed + ti.offset + (size_t)slab0 * ti.chunk_bytes;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // Weights do not depend on the previous kernel: start streaming them
-      // before waiting for the activations (programmatic dependent launch).
-      int issued = 0;
-      for (int i = 0; i < nsl && i < RS; ++i) {
+    // Converged warp; the elected lane issues the copies. Weights do not
+    // depend on the previous kernel: start streaming them before waiting for
+    // the activations (programmatic dependent launch).
+    int issued = 0;
+    for (int i = 0; i < nsl && i < RS; ++i) {
+      if (dev::elect_one()) {
         dev::mbar_arrive_expect_tx(rfull + 8 * i, ti.chunk_bytes);
         dev::bulk_load(dev::smem_u32(raw + i * a.chunk_max), chunk0 + (size_t)i * ti.chunk_bytes, ti.chunk_bytes,
                        rfull + 8 * i);
-        ++issued;
       }
-      dev::pdl_wait();
+      __syncwarp();
+      ++issued;
+    }
+    dev::pdl_wait();
+    if (dev::elect_one()) {
       dev::mbar_arrive_expect_tx(xfull, (uint32_t)(kr / 64) * NP * 128);
       for (int c = 0; c < kr / 64; ++c)
         dev::tma_load_2d(dev::smem_u32(xs + c * NP * 128), &map_x, slab0 * 256 + c * 64, 0, xfull);
-      for (int i = RS; i < nsl; ++i) {
-        const int s = i % RS;
-        if (!dev::mbar_wait(rempty + 8 * s, ((i / RS) & 1) ^ 1, a.err)) break;
+    }
+    __syncwarp();
+    for (int i = RS; i < nsl; ++i) {
+      const int s = i % RS;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(rempty + 8 * s, ((i / RS) & 1) ^ 1, a.err))) break;
+      if (dev::elect_one()) {
         dev::mbar_arrive_expect_tx(rfull + 8 * s, ti.chunk_bytes);
         dev::bulk_load(dev::smem_u32(raw + s * a.chunk_max), chunk0 + (size_t)i * ti.chunk_bytes, ti.chunk_bytes,
                        rfull + 8 * s);
-        ++issued;
       }
-      // Drain: every issued copy has landed before shared memory is reused.
-      dev::mbar_wait(xfull, 0, a.err, 100000000ull);
-      for (int i = issued > RS ? issued - RS : 0; i < issued; ++i)
-        dev::mbar_wait(rfull + 8 * (i % RS), (i / RS) & 1, a.err, 100000000ull);
+      __syncwarp();
+      ++issued;
     }
+    // Drain: every issued copy has landed before shared memory is reused.
+    dev::mbar_wait(xfull, 0, a.err, 100000000ull);
+    for (int i = issued > RS ? issued - RS : 0; i < issued; ++i)
+      dev::mbar_wait(rfull + 8 * (i % RS), (i / RS) & 1, a.err, 100000000ull);
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
-      if (dev::mbar_wait(xfull, 0, a.err)) {
-        const uint32_t xbase = dev::smem_u32(xs), abase = dev::smem_u32(as);
-        int sub = 0;
-        bool ok = true;
-        for (int i = 0; i < nsl && ok; ++i)
-          for (int q = 0; q < 4; ++q, ++sub) {
-            const int s = sub % kAStages;
-            if (!dev::mbar_wait(afull + 8 * s, (sub / kAStages) & 1, a.err)) {
-              ok = false;
-              break;
-            }
-            dev::tc_fence_after();
+    // Converged warp; the elected lane (lane 0) issues every MMA and commit.
+    constexpr uint32_t idesc = dev::make_idesc_f16(128, NP);
+    if (__all_sync(0xffffffffu, dev::mbar_wait(xfull, 0, a.err))) {
+      const uint32_t xbase = dev::smem_u32(xs), abase = dev::smem_u32(as);
+      int sub = 0;
+      bool ok = true;
+      for (int i = 0; i < nsl && ok; ++i)
+        for (int q = 0; q < 4; ++q, ++sub) {
+          const int s = sub % kAStages;
+          if (!__all_sync(0xffffffffu, dev::mbar_wait(afull + 8 * s, (sub / kAStages) & 1, a.err))) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
+            if (dev::elect_one()) {
               const uint64_t ad = dev::make_sw128_desc(abase + s * kABytes + kk * 32);
               const uint64_t bd = dev::make_sw128_desc(xbase + (i * 4 + q) * NP * 128 + kk * 32);
               dev::tc_mma_f16(tmem, ad, bd, idesc, (sub | kk) != 0 ? 1u : 0u);
             }
-            dev::tc_commit(aempty + 8 * s);
+            __syncwarp();
           }
-      }
-      dev::tc_commit(accum);
-      dev::mbar_wait(accum, 0, a.err, 100000000ull);
+          if (dev::elect_one()) dev::tc_commit(aempty + 8 * s);
+          __syncwarp();
+        }
     }
+    if (dev::elect_one()) dev::tc_commit(accum);
+    __syncwarp();
+    dev::mbar_wait(accum, 0, a.err, 100000000ull);
   } else {
     // ---- decoders: thread = weight row of the tile ----
     const int r = threadIdx.x - 64;
