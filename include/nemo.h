@@ -100,6 +100,13 @@ void* nemo_plan_stream(nemo_plan* plan);
  * the reference has no counterpart. */
 int nemo_plan_single_launch(nemo_plan* plan);
 
+/* For a plan of batch 1 on 2, 4 or 8 devices: the request length from which
+ * nemo_plan_run runs the request head-parallel across the devices (token-
+ * sharded projections, NCCL all-to-all around attention); 0 when the plan has
+ * no head-parallel path. Default 5000 tokens, NEMO_HEAD_PARALLEL_MIN at plan
+ * creation overrides. Build-specific introspection; no reference counterpart. */
+int nemo_plan_head_parallel(nemo_plan* plan);
+
 /* Waits for the plan's streams; returns NEMO_ERR_TIMEOUT if a kernel reported
  * a bounded wait giving up. */
 int nemo_plan_synchronize(nemo_plan* plan);

@@ -96,6 +96,14 @@ int nemo_plan_single_launch(nemo_plan* plan) {
   return 1;
 }
 
+int nemo_plan_head_parallel(nemo_plan* plan) {
+  if (!plan) {
+    nemo::set_error("nemo_plan_head_parallel: null plan");
+    return nemo::kErrArgs;
+  }
+  return plan->hp ? plan->hp_min : 0;
+}
+
 int nemo_plan_profile(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
                       float* stage_ms) {
   return plan_profile(plan, ids, n_ids, lengths, n_lengths, stage_ms);

@@ -51,6 +51,8 @@ struct AttnTcArgs {
   int merged;
   __half* out;
   uint32_t* err;
+  int v_col0;  // column of the head group's V in the rows of the v map
+  int out_ld;  // output row stride (q heads of the group x 128)
 };
 
 __global__ void __launch_bounds__(192, 1)
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(192, 1)
   const CUtensorMap* km = sampled ? &map_kc : &map_k;
   const CUtensorMap* vm = sampled ? &map_vc : &map_v;
   const int kcol = kvh * kHeadDim;
-  const int vcol = sampled ? kvh * kHeadDim : kQWidth + kKVWidth + kvh * kHeadDim;
+  const int vcol = sampled ? kvh * kHeadDim : a.v_col0 + kvh * kHeadDim;
   const int ntiles = (nkeys + kTile - 1) / kTile;
 
   const uint32_t raw_s = dev::smem_u32(smem_raw);
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(192, 1)
     if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done, (ntiles - 1) & 1, a.err))) {
       dev::tc_fence_after();
       const float inv = 1.0f / l;
-      __half* dst = a.out + (size_t)(base + pos) * kQWidth + h * kHeadDim;
+      __half* dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
@@ -297,11 +299,14 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // Gathers every third key of the requests whose valid length exceeds 2048
-// into compact K/V buffers (one 256-thread block per compact row).
+// into compact K/V buffers (one block per compact row, 8 columns per thread).
+// kv_w = KV heads of the group x 128; k rows are kv_w wide, V sits at column
+// v_col0 of qkv rows qkv_ld wide.
 __global__ void __launch_bounds__(128) gather_sampled_kernel(const __half* __restrict__ k,
                                                             const __half* __restrict__ qkv,
                                                             const Meta* __restrict__ meta, int merged,
-                                                            __half* kc, __half* vc) {
+                                                            __half* kc, __half* vc, int kv_w, int qkv_ld,
+                                                            int v_col0) {
   const int ph = merged ? 1 : 0;
   const int row = blockIdx.x;
   if (row >= meta->samp_off[ph][meta->batch]) return;
@@ -309,25 +314,41 @@ __global__ void __launch_bounds__(128) gather_sampled_kernel(const __half* __res
   while (b + 1 < meta->batch && row >= meta->samp_off[ph][b + 1]) ++b;
   const int base = merged ? meta->tgt_off[b] : meta->src_off[b];
   const size_t src = (size_t)base + (size_t)(row - meta->samp_off[ph][b]) * kSampleStride;
-  const int c = threadIdx.x * 8;  // 128 threads x 8 = 1024 columns (8 kv heads x 128)
-  *reinterpret_cast<uint4*>(kc + (size_t)row * kKVWidth + c) =
-      *reinterpret_cast<const uint4*>(k + src * kKVWidth + c);
-  *reinterpret_cast<uint4*>(vc + (size_t)row * kKVWidth + c) =
-      *reinterpret_cast<const uint4*>(qkv + src * kQKVWidth + kQWidth + kKVWidth + c);
+  const int c = threadIdx.x * 8;
+  if (c >= kv_w) return;
+  *reinterpret_cast<uint4*>(kc + (size_t)row * kv_w + c) = *reinterpret_cast<const uint4*>(k + src * kv_w + c);
+  *reinterpret_cast<uint4*>(vc + (size_t)row * kv_w + c) =
+      *reinterpret_cast<const uint4*>(qkv + src * qkv_ld + v_col0 + c);
 }
 
 }  // namespace
 
 cudaError_t launch_gather_sampled(const __half* k, const __half* qkv, const Meta* meta, bool merged, int max_rows,
                                   __half* kc, __half* vc, cudaStream_t s) {
+  return launch_gather_sampled_group(k, qkv, kQKVWidth, kQWidth + kKVWidth, kKVWidth, meta, merged, max_rows, kc, vc,
+                                     s);
+}
+
+cudaError_t launch_gather_sampled_group(const __half* k, const __half* qkv, int qkv_ld, int v_col0, int kv_w,
+                                        const Meta* meta, bool merged, int max_rows, __half* kc, __half* vc,
+                                        cudaStream_t s) {
   if (max_rows <= 0) return cudaSuccess;
-  gather_sampled_kernel<<<max_rows, 128, 0, s>>>(k, qkv, meta, merged ? 1 : 0, kc, vc);
+  if (kv_w % 8 || kv_w > 1024 || v_col0 % 8 || qkv_ld % 8) return cudaErrorInvalidValue;
+  gather_sampled_kernel<<<max_rows, 128, 0, s>>>(k, qkv, meta, merged ? 1 : 0, kc, vc, kv_w, qkv_ld, v_col0);
   return cudaGetLastError();
 }
 
 cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
                                 __half* out, uint32_t* err, cudaStream_t s) {
+  return launch_attention_tc_group(maps, meta, merged, batch, max_len, kQHeads, kQWidth + kKVWidth, kQWidth, out, err,
+                                   s);
+}
+
+cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
+                                      int q_heads, int v_col0, int out_ld, __half* out, uint32_t* err,
+                                      cudaStream_t s) {
   if (max_len <= 0 || batch <= 0) return cudaSuccess;
+  if (q_heads <= 0 || q_heads % (kQHeads / kKVHeads) || v_col0 % 8 || out_ld % 8) return cudaErrorInvalidValue;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -338,8 +359,8 @@ cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool mer
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  AttnTcArgs a{meta, merged ? 1 : 0, out, err};
-  dim3 grid((max_len + kTile - 1) / kTile, kQHeads, batch);
+  AttnTcArgs a{meta, merged ? 1 : 0, out, err, v_col0, out_ld};
+  dim3 grid((max_len + kTile - 1) / kTile, q_heads, batch);
   attention_tc_kernel<<<grid, 192, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
   return cudaGetLastError();
 }

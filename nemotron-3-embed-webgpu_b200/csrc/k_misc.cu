@@ -247,31 +247,34 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(__half* x, const __half* _
 }
 
 // ops.ts:168-194: one thread per (token, head, pair); the position is the
-// token's index within its (merged) row.
+// token's index within its (merged) row. A head group of nq q heads and nk kv
+// heads: Q at columns [0, nq*128) and K at [nq*128, (nq+nk)*128) of qkv rows
+// qkv_ld wide (the full model: 24, 8, 5120).
 __global__ void __launch_bounds__(256) rope_kernel(const __half* __restrict__ qkv,
                                                    const float* __restrict__ table,
                                                    const Meta* __restrict__ meta, int merged, __half* q,
-                                                   __half* k) {
+                                                   __half* k, int nq, int nk, int qkv_ld) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int tok = (int)(idx >> 11);
+  const int per_tok = (nq + nk) * 64;
+  const int tok = (int)(idx / per_tok);
   const int T = merged ? meta->t1 : meta->t0;
   if (tok >= T) return;
-  const int hp = (int)(idx & 2047), head = hp >> 6, pair = hp & 63;
+  const int hp = (int)(idx - (long long)tok * per_tok), head = hp >> 6, pair = hp & 63;
   const int* off = merged ? meta->tgt_off : meta->src_off;
   const int b = find_request(off, meta->batch, tok);
   const int pos = tok - off[b];
-  const bool is_q = head < kQHeads;
-  const int col = is_q ? head * kHeadDim : kQWidth + (head - kQHeads) * kHeadDim;
-  const __half2 in = *reinterpret_cast<const __half2*>(qkv + (size_t)tok * kQKVWidth + col + pair * 2);
+  const bool is_q = head < nq;
+  const int col = head * kHeadDim;
+  const __half2 in = *reinterpret_cast<const __half2*>(qkv + (size_t)tok * qkv_ld + col + pair * 2);
   const float2 cs = *reinterpret_cast<const float2*>(table + ((size_t)pos * 64 + pair) * 2);
   const float even = __low2float(in), odd = __high2float(in);
   const float first = __fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y));
   const float second = __fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x));
   const __half2 o = __halves2half2(__float2half_rn(first), __float2half_rn(second));
   if (is_q)
-    *reinterpret_cast<__half2*>(q + ((size_t)tok * kQHeads + head) * kHeadDim + pair * 2) = o;
+    *reinterpret_cast<__half2*>(q + ((size_t)tok * nq + head) * kHeadDim + pair * 2) = o;
   else
-    *reinterpret_cast<__half2*>(k + ((size_t)tok * kKVHeads + head - kQHeads) * kHeadDim + pair * 2) = o;
+    *reinterpret_cast<__half2*>(k + ((size_t)tok * nk + head - nq) * kHeadDim + pair * 2) = o;
 }
 
 // ops.ts:74-89: out = f16(silu(g) * u), silu = g / (1 + exp(-g)).
@@ -440,8 +443,15 @@ cudaError_t launch_residual_rmsnorm(__half* x, const __half* residual, const flo
 
 cudaError_t launch_rope(const __half* qkv, const float* table, const Meta* meta, bool merged, int max_tokens,
                         __half* q, __half* k, cudaStream_t s) {
-  const long long threads = (long long)max_tokens * 2048;
-  rope_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(qkv, table, meta, merged ? 1 : 0, q, k);
+  return launch_rope_group(qkv, kQKVWidth, kQHeads, kKVHeads, table, meta, merged, max_tokens, q, k, s);
+}
+
+cudaError_t launch_rope_group(const __half* qkv, int qkv_ld, int nq, int nk, const float* table, const Meta* meta,
+                              bool merged, int max_tokens, __half* q, __half* k, cudaStream_t s) {
+  if (max_tokens <= 0) return cudaSuccess;
+  const long long threads = (long long)max_tokens * (nq + nk) * 64;
+  rope_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(qkv, table, meta, merged ? 1 : 0, q, k, nq, nk,
+                                                                qkv_ld);
   return cudaGetLastError();
 }
 

@@ -50,6 +50,10 @@ cudaError_t launch_residual_rmsnorm(__half* x, const __half* residual, const flo
 // ops.ts:168-194. merged selects the post-merge offsets for positions.
 cudaError_t launch_rope(const __half* qkv, const float* table, const Meta* meta, bool merged,
                         int max_tokens, __half* q, __half* k, cudaStream_t s);
+// Same for a head group: Q at columns [0, nq*128), K at [nq*128, (nq+nk)*128)
+// of qkv rows qkv_ld wide; q out [T x nq x 128], k out [T x nk x 128].
+cudaError_t launch_rope_group(const __half* qkv, int qkv_ld, int nq, int nk, const float* table, const Meta* meta,
+                              bool merged, int max_tokens, __half* q, __half* k, cudaStream_t s);
 
 // ops.ts:213-362. q [T x 24 x 128], k [T x 8 x 128], v read from qkv at column
 // 4096 (row stride 5120); out [T x 3072].
@@ -67,6 +71,14 @@ cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool mer
                                 __half* out, uint32_t* err, cudaStream_t s);
 cudaError_t launch_gather_sampled(const __half* k, const __half* qkv, const Meta* meta, bool merged, int max_rows,
                                   __half* kc, __half* vc, cudaStream_t s);
+// Head-group variants (head-parallel attention): q_heads q heads with their
+// q_heads/3 kv heads; V at column v_col0 of the v map's rows; out rows out_ld wide.
+cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
+                                      int q_heads, int v_col0, int out_ld, __half* out, uint32_t* err,
+                                      cudaStream_t s);
+cudaError_t launch_gather_sampled_group(const __half* k, const __half* qkv, int qkv_ld, int v_col0, int kv_w,
+                                        const Meta* meta, bool merged, int max_rows, __half* kc, __half* vc,
+                                        cudaStream_t s);
 
 // ops.ts:74-89 over [rows x 12288] -> [rows x 6144].
 cudaError_t launch_swiglu(const __half* gate_up, const int* d_rows, int max_rows, __half* out,

@@ -554,12 +554,27 @@ int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out) {
       return rc;
     }
   }
+  // Multi-device plans of one request: from hp_min tokens on (default 5000,
+  // NEMO_HEAD_PARALLEL_MIN overrides) the request runs head-parallel.
+  if (plan->devs.size() >= 2 && batch == 1) {
+    const char* env = getenv("NEMO_HEAD_PARALLEL_MIN");
+    plan->hp_min = env ? std::max(1, atoi(env)) : 5000;
+    if ((int)seq >= plan->hp_min) {
+      if (int rc = hp_create(plan, &plan->hp)) {
+        for (auto& d : plan->devs) free_device_plan(*d);
+        delete plan;
+        return rc;
+      }
+    }
+  }
   *out = plan;
   return kOk;
 }
 
 void plan_destroy(nemo_plan* plan) {
   if (!plan) return;
+  hp_destroy(plan->hp);
+  plan->hp = nullptr;
   for (auto& d : plan->devs) {
     cudaSetDevice(d->device);
     cudaStreamSynchronize(d->stream);
@@ -616,6 +631,7 @@ int plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t*
   }
   if (int rc = validate_inputs(plan, ids, n_ids, lengths, n_lengths)) return rc;
   const int ndev = (int)plan->devs.size();
+  if (plan->hp && (int)lengths[0] >= plan->hp_min) return hp_run(plan, plan->hp, ids, (int)lengths[0], out);
   // Request sharding: longest first onto the device with the fewest tokens.
   std::vector<std::vector<int>> assign(ndev);
   if (ndev == 1) {

@@ -129,8 +129,20 @@ struct nemo_model {
   uint64_t packed_bytes = 0;
 };
 
+namespace nemo {
+// Head-parallel forward of one long request across a plan's devices (headpar.cu).
+struct HeadPar;
+int hp_create(nemo_plan* plan, HeadPar** out);
+int hp_run(nemo_plan* plan, HeadPar* hp, const uint32_t* ids, int len, float* out);
+void hp_destroy(HeadPar* hp);
+}  // namespace nemo
+
 struct nemo_plan {
   nemo_model* model = nullptr;
   int batch = 0, seq = 0;
   std::vector<std::unique_ptr<nemo::DevicePlan>> devs;
+  // Multi-device plans of batch 1: requests of at least hp_min tokens run
+  // head-parallel over all devices (NCCL); shorter ones run on one device.
+  nemo::HeadPar* hp = nullptr;
+  int hp_min = 0;
 };

@@ -59,6 +59,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_plan_run_device": (I, [P, P, P, P]),
         "nemo_plan_stream": (P, [P]),
         "nemo_plan_single_launch": (I, [P]),
+        "nemo_plan_head_parallel": (I, [P]),
         "nemo_plan_synchronize": (I, [P]),
         "nemo_plan_profile": (I, [P, P, S, P, S, P]),
         "nemo_stage_name": (ctypes.c_char_p, [I]),
@@ -142,6 +143,15 @@ class NemotronExecutionPlan:
 
     def stream(self) -> int:
         return load_library().nemo_plan_stream(self._h) or 0
+
+    @property
+    def head_parallel_min(self) -> int:
+        """Request length from which runs go head-parallel over the plan's
+        devices (0: the plan has no head-parallel path)."""
+        r = load_library().nemo_plan_head_parallel(self._h)
+        if r < 0:
+            check(r)
+        return r
 
     @property
     def fused(self) -> bool:

@@ -32,3 +32,37 @@ def test_two_device_plan_matches_single_device():
     for i in range(len(reqs)):
         cos = float(a[i] @ b[i] / (np.linalg.norm(a[i]) * np.linalg.norm(b[i])))
         assert cos >= 0.9999, (i, cos)
+
+
+@pytest.mark.parametrize("length", [700, 2300])
+def test_head_parallel_matches_single_device(length, monkeypatch):
+    """One long request on a two-device plan runs head-parallel (token-sharded
+    projections, NCCL all-to-all around attention, all-gathers for the merge
+    and the pool); 2300 tokens also samples every third key before the merge.
+    The embedding must match the single-device run."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = synth.cached_model_pack(3, "kquant", 5)
+    with open(path, "rb") as f:
+        data = f.read()
+    reqs = synth.make_requests(9, [length], vocab=synth.VOCAB)
+    ids, lens, seq = synth.pad_batch(reqs)
+    one = NemotronB200Model(data, devices=[0])
+    two = NemotronB200Model(data, devices=[0, 1])
+    try:
+        monkeypatch.setenv("NEMO_HEAD_PARALLEL_MIN", "512")
+        plan2 = two.create_plan(1, seq)
+        assert plan2.head_parallel_min == 512
+        b = plan2.run_array(ids, lens).copy()
+        b2 = plan2.run_array(ids, lens).copy()
+        plan1 = one.create_plan(1, seq)
+        assert plan1.head_parallel_min == 0
+        a = plan1.run_array(ids, lens).copy()
+    finally:
+        one.destroy()
+        two.destroy()
+    assert np.array_equal(b, b2)
+    cos = float(a[0] @ b[0] / (np.linalg.norm(a[0]) * np.linalg.norm(b[0])))
+    assert cos >= 0.9999, cos
+    assert abs(np.linalg.norm(b[0]) - 1) < 1e-3
