@@ -520,6 +520,10 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         float* dst = stage + pt * 4;
         const int n = (kHidden / 128) * sst * 32;  // 16-byte chunks of the row's block
         for (int k = pt; k < n; k += 128, src += 512, dst += 512) cp_async16(dst, src);
+        // the residual row joins the same batch of copies
+        const __half* xr = x + (size_t)t * kHidden;
+        __half* xs = reinterpret_cast<__half*>(stage + (kHidden / 128) * sst * 128);
+        for (int k = pt; k < kHidden / 8; k += 128) cp_async16(xs + k * 8, xr + k * 8);
         cp_async_wait_all();
         pw_sync();
       }
@@ -528,7 +532,11 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = h * 1024 + pt * 8;
-        unpack8(__ldcg(reinterpret_cast<const uint4*>(x + (size_t)t * kHidden + c)), v[h]);
+        if (res)
+          unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(stage + (kHidden / 128) * sst * 128) + c),
+                  v[h]);
+        else
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(x + (size_t)t * kHidden + c)), v[h]);
         if (res) {
           const int tile = c >> 7, S = nslots[rpi * kFwdMaxTiles + tile];
           const float* p = stage + tile * sst * 128 + (c & 127);
@@ -652,77 +660,111 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       projection(l * 4 + 0, &a.xmap[merged ? 1 : 0], merged);
       grid_barrier();
 
-      // ---- attention (ops.ts:295-362): one (request, q head) per item. Each
-      // warp scores its queries (4 dims per lane, butterfly sums) and keeps the
-      // softmax row in shared memory; then thread d accumulates dimension d of
-      // every query's output. ----
+      // ---- QKV outputs (ops.ts:168-194): the projection's partial slots summed
+      // in K order, f16, RoPE on Q and K (position = row within the request);
+      // spread over the grid, item = (128-column tile, token), thread = column.
+      // Up to four items per pass keep all their slot loads in flight. ----
+      {
+        const int qkv_pi = l * 4, ss = sstride[qkv_pi];
+        const int* off = merged ? meta->tgt_off : meta->src_off;
+        const uint8_t* ns = nslots + qkv_pi * kFwdMaxTiles;
+        constexpr int kTiles = kQKVWidth / 128, kItemsPerPass = 4, kSlotRegs = 8;
+        const int n_items = kTiles * T;
+        for (int i0 = cta; i0 < n_items; i0 += kItemsPerPass * G) {
+          float v[kItemsPerPass][kSlotRegs];
+#pragma unroll
+          for (int k = 0; k < kItemsPerPass; ++k) {
+            const int item = i0 + k * G;
+            const int tile = item % kTiles, t = item / kTiles;
+            const int S = item < n_items ? ns[tile] : 0;
+            const float* p = a.part + ((size_t)tile * NP + t) * ss * 128 + pt;
+#pragma unroll
+            for (int sl = 0; sl < kSlotRegs; ++sl) v[k][sl] = sl < S ? __ldcg(p + sl * 128) : 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < kItemsPerPass; ++k) {
+            const int item = i0 + k * G;
+            if (item >= n_items) break;  // uniform over the CTA
+            const int tile = item % kTiles, t = item / kTiles;
+            const int S = ns[tile];
+            const float* p = a.part + ((size_t)tile * NP + t) * ss * 128 + pt;
+            float acc = 0.f;
+#pragma unroll
+            for (int sl = 0; sl < kSlotRegs; ++sl)
+              if (sl < S) acc = __fadd_rn(acc, v[k][sl]);
+            for (int sl = kSlotRegs; sl < S; ++sl) acc = __fadd_rn(acc, __ldcg(p + sl * 128));
+            const float val = __half2float(__float2half_rn(acc));
+            const int col = tile * 128 + pt;
+            if (col < kQWidth + kKVWidth) {
+              const float other = __shfl_xor_sync(0xffffffffu, val, 1);  // the pair partner (adjacent column)
+              const bool odd = pt & 1;
+              const float even_v = odd ? other : val, odd_v = odd ? val : other;
+              const int b = find_req(off, batch, t);
+              const float2 cs = *reinterpret_cast<const float2*>(rope + ((t - off[b]) * 64 + ((col & 127) >> 1)) * 2);
+              const float r = odd ? __fadd_rn(__fmul_rn(even_v, cs.y), __fmul_rn(odd_v, cs.x))
+                                  : __fsub_rn(__fmul_rn(even_v, cs.x), __fmul_rn(odd_v, cs.y));
+              if (col < kQWidth) a.q[(size_t)t * kQWidth + col] = __float2half_rn(r);
+              else a.k[(size_t)t * kKVWidth + col - kQWidth] = __float2half_rn(r);
+            } else {
+              a.qkv[(size_t)t * kQKVWidth + col] = __float2half_rn(val);
+            }
+          }
+        }
+      }
+      grid_barrier();
+
+      // ---- attention (ops.ts:295-362): item = (request, q head, group of up
+      // to 8 queries). Thread per (query, key) score with four partial sums,
+      // softmax per query row, then thread d accumulates dimension d of each
+      // query's output. ----
       {
         float* ks = reinterpret_cast<float*>(xring);  // [NP][128]
         float* vs = ks + NP * kHeadDim;                // [NP][128]
-        float* qs = vs + NP * kHeadDim;                // [NP][128]
-        float* ps = qs + NP * kHeadDim;                // [NP][NP]
-        float* linv = ps + NP * NP;                    // [NP]
+        float* qs = vs + NP * kHeadDim;                // [8][128]
+        float* ps = qs + 8 * kHeadDim;                 // [8][NP]
+        float* linv = ps + 8 * NP;                     // [8]
         const int* off = merged ? meta->tgt_off : meta->src_off;
-        const int qkv_pi = l * 4;
+        constexpr int kQG = 8, kGroups = (NP + kQG - 1) / kQG;
         set_quiet(true);
-        for (int item = cta; item < batch * kQHeads; item += G) {
-          const int b = item / kQHeads, h = item % kQHeads, kvh = h / (kQHeads / kKVHeads);
+        for (int item = cta; item < batch * kQHeads * kGroups; item += G) {
+          const int b = item / (kQHeads * kGroups), rem = item % (kQHeads * kGroups);
+          const int h = rem / kGroups, g = rem % kGroups, kvh = h / (kQHeads / kKVHeads);
           const int len = min(merged ? meta->tgt_len[b] : meta->src_len[b], NP);
+          const int q0 = g * kQG, nq = min(kQG, len - q0);
+          if (nq <= 0) continue;  // uniform over the CTA
           const int base = off[b];
-          // Q (tile h), K (tile 24 + kvh) and V (tile 32 + kvh) of the
-          // request's rows from the QKV partial slots, staged into the slot
-          // buffers in as few rounds as fit: f16 QKV, then RoPE on Q and K
-          // (ops.ts:168-194; position = row within the request).
-          const uint8_t* ns = nslots + qkv_pi * kFwdMaxTiles;
-          const int tiles[3] = {h, kQHeads + kvh, kQHeads + kKVHeads + kvh};
-          const int ss = sstride[qkv_pi];
-          const int cap = a.max_slots * NP;  // 128-float rows of the slot buffers
-          for (int p0 = 0; p0 < 3;) {
-            int p1 = p0;
-            while (p1 < 3 && (p1 == p0 || (p1 + 1 - p0) * ss * len <= cap)) ++p1;
-            const int per = len * ss * 32;  // 16-byte chunks per part: the request's rows, all slots
-            for (int pp = p0; pp < p1; ++pp) {
-              const float* src = a.part + ((size_t)tiles[pp] * NP + base) * ss * 128 + pt * 4;
-              float* dst = ebuf + (pp - p0) * len * ss * 128 + pt * 4;
-              for (int k = pt; k < per; k += 128, src += 512, dst += 512) cp_async16(dst, src);
+          // K and V rows of the request, Q rows of the group: every load is
+          // issued before the first shared-memory store
+          constexpr int kLoads = ((2 * NP + kQG) * 16 + 127) / 128;
+          uint4 buf[kLoads];
+          float* dsts[kLoads];
+#pragma unroll
+          for (int k = 0; k < kLoads; ++k) {
+            const int u = pt + k * 128, row = u >> 4, c = (u & 15) * 8;
+            dsts[k] = nullptr;
+            if (row < len) {
+              buf[k] = __ldcg(reinterpret_cast<const uint4*>(a.k + ((size_t)(base + row) * kKVHeads + kvh) * kHeadDim + c));
+              dsts[k] = ks + row * kHeadDim + c;
+            } else if (row < 2 * len) {
+              buf[k] = __ldcg(reinterpret_cast<const uint4*>(a.qkv + (size_t)(base + row - len) * kQKVWidth + kQWidth +
+                                                             kKVWidth + kvh * kHeadDim + c));
+              dsts[k] = vs + (row - len) * kHeadDim + c;
+            } else if (row < 2 * len + nq) {
+              buf[k] = __ldcg(reinterpret_cast<const uint4*>(a.q + ((size_t)(base + q0 + row - 2 * len) * kQHeads + h) * kHeadDim + c));
+              dsts[k] = qs + (row - 2 * len) * kHeadDim + c;
             }
-            cp_async_wait_all();
-            pw_sync();
-            for (int pp = p0; pp < p1; ++pp)
-            for (int u = pt; u < len * 16; u += 128) {
-              const int j = u >> 4, c = (u & 15) * 8;
-              const int S = ns[tiles[pp]];
-              float v8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-              for (int sl = 0; sl < S; ++sl) {
-                const float* q8 = ebuf + (((pp - p0) * len + j) * ss + sl) * 128 + c;
-                const float4 u0 = *reinterpret_cast<const float4*>(q8);
-                const float4 u1 = *reinterpret_cast<const float4*>(q8 + 4);
-                const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v8[e] = __fadd_rn(v8[e], uu[e]);
-              }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v8[e] = __half2float(__float2half_rn(v8[e]));
-              float* dst = (pp == 0 ? qs : pp == 1 ? ks : vs) + j * kHeadDim + c;
-              if (pp < 2) {
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                  const float2 cs = *reinterpret_cast<const float2*>(rope + (j * 64 + ((c + e) >> 1)) * 2);
-                  dst[e] = __half2float(__float2half_rn(__fsub_rn(__fmul_rn(v8[e], cs.x), __fmul_rn(v8[e + 1], cs.y))));
-                  dst[e + 1] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(v8[e], cs.y), __fmul_rn(v8[e + 1], cs.x))));
-                }
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) dst[e] = v8[e];
-              }
-            }
-            pw_sync();  // the slot buffers are refilled by the next round
-            p0 = p1;
           }
+#pragma unroll
+          for (int k = 0; k < kLoads; ++k)
+            if (dsts[k]) {
+              float f[8];
+              unpack8(buf[k], f);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) dsts[k][e] = f[e];
+            }
+          pw_sync();
           const float scale = 0.08838834764831845f;
-          // scores: thread per (query, key) pair, four independent partial
-          // sums over dimensions (start staggered by key: no bank conflicts)
-          for (int e = pt; e < len * len; e += 128) {
+          for (int e = pt; e < nq * len; e += 128) {
             const int i = e / len, j = e - i * len;
             float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
@@ -735,11 +777,12 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
               s4[2] = fmaf(q4.z, k4.z, s4[2]);
               s4[3] = fmaf(q4.w, k4.w, s4[3]);
             }
-            const float temp = i >= 16384 ? logf(floorf((float)i / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
+            const int pos = q0 + i;
+            const float temp = pos >= 16384 ? logf(floorf((float)pos / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
             ps[i * NP + j] = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale * temp;
           }
           pw_sync();
-          if (pt < len) {  // softmax of query row pt
+          if (pt < nq) {  // softmax of query row pt
             float m = -INFINITY;
             for (int j = 0; j < len; ++j) m = fmaxf(m, ps[pt * NP + j]);
             float l = 0.f;
@@ -751,17 +794,18 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
             linv[pt] = 1.0f / l;
           }
           pw_sync();
-          float acc[NP];
+          float acc[kQG];
 #pragma unroll
-          for (int i = 0; i < NP; ++i) acc[i] = 0.f;
+          for (int i = 0; i < kQG; ++i) acc[i] = 0.f;
           for (int j = 0; j < len; ++j) {
             const float v = vs[j * kHeadDim + pt];
 #pragma unroll
-            for (int i = 0; i < NP; ++i) acc[i] = fmaf(ps[i * NP + j], v, acc[i]);
+            for (int i = 0; i < kQG; ++i) acc[i] = fmaf(ps[i * NP + j], v, acc[i]);
           }
 #pragma unroll
-          for (int i = 0; i < NP; ++i)
-            if (i < len) a.attn[(size_t)(base + i) * kQWidth + h * kHeadDim + pt] = __float2half_rn(acc[i] * linv[i]);
+          for (int i = 0; i < kQG; ++i)
+            if (i < nq)
+              a.attn[(size_t)(base + q0 + i) * kQWidth + h * kHeadDim + pt] = __float2half_rn(acc[i] * linv[i]);
           pw_sync();
         }
         set_quiet(false);
