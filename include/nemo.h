@@ -69,6 +69,16 @@ int nemo_model_info_get(const nemo_model* model, nemo_model_info* info);
  * batch in [1, 16], sequence in [1, NEMO_MAX_SEQUENCE]. */
 int nemo_plan_create(nemo_model* model, uint32_t batch, uint32_t sequence, nemo_plan** out);
 
+/* Plan flags for nemo_plan_create_ex. */
+#define NEMO_PLAN_EXACT_ATTENTION 1u /* no layer-4 token merge, no stride-3 key sampling */
+
+/* nemo_plan_create with flags (0 = the reference's semantics). With
+ * NEMO_PLAN_EXACT_ATTENTION every layer keeps all valid tokens and attends over
+ * every valid key: the reference's two approximations (model.ts:157 merge,
+ * ops.ts:258-269 sampling) are off. No reference counterpart; single-request
+ * runs on several devices stay on one device in this mode. */
+int nemo_plan_create_ex(nemo_model* model, uint32_t batch, uint32_t sequence, uint32_t flags, nemo_plan** out);
+
 /* Runs one micro-batch and blocks until the embeddings are in `out`.
  * Replaces NemotronExecutionPlan.run (src/webgpu/model.ts:146-176) /
  * EmbeddingPlan.run (src/webgpu/embedding-engine.ts:7-9).

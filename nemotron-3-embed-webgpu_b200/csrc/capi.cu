@@ -16,7 +16,7 @@ const char* last_error() { return g_last_error.c_str(); }
 
 int model_load(const void* data, size_t bytes, const int* devices, int ndev, nemo_model** out);
 void model_destroy(nemo_model* m);
-int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out);
+int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, uint32_t flags, nemo_plan** out);
 void plan_destroy(nemo_plan* plan);
 int plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
              float* out);
@@ -68,7 +68,15 @@ int nemo_model_info_get(const nemo_model* m, nemo_model_info* info) {
 }
 
 int nemo_plan_create(nemo_model* model, uint32_t batch, uint32_t sequence, nemo_plan** out) {
-  return plan_create(model, batch, sequence, out);
+  return plan_create(model, batch, sequence, 0, out);
+}
+
+int nemo_plan_create_ex(nemo_model* model, uint32_t batch, uint32_t sequence, uint32_t flags, nemo_plan** out) {
+  if (flags & ~(uint32_t)NEMO_PLAN_EXACT_ATTENTION) {
+    nemo::set_error("nemo_plan_create_ex: unknown flags");
+    return nemo::kErrArgs;
+  }
+  return plan_create(model, batch, sequence, flags, out);
 }
 
 int nemo_plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,

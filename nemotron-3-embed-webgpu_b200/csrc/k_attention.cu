@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
   if (q0 >= len) return;
   const int base = off[b];
   const int kvh = h / (kQHeads / kKVHeads);
-  const int stride = len > 2048 ? 3 : 1;
+  const int stride = !meta->exact && len > 2048 ? 3 : 1;
   const int nkeys = (len + stride - 1) / stride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 

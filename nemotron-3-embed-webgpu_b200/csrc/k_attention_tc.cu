@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(192, 1)
   if (q0 >= len) return;  // uniform over the CTA
   const int base = a.merged ? meta->tgt_off[b] : meta->src_off[b];
   const int kvh = h / (kQHeads / kKVHeads);
-  const bool sampled = len > kSampleThreshold;
+  const bool sampled = !meta->exact && len > kSampleThreshold;
   const int nkeys = sampled ? (len + kSampleStride - 1) / kSampleStride : len;
   const int kbase = sampled ? meta->samp_off[ph][b] : base;
   const CUtensorMap* km = sampled ? &map_kc : &map_k;

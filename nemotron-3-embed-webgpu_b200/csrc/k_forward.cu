@@ -611,8 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     grid_barrier();
 
     for (int l = 0; l < a.n_layers; ++l) {
-      const bool merged = l >= kMergeAfterLayer;
-      if (l == kMergeAfterLayer) {
+      const bool merged = !a.exact && l >= kMergeAfterLayer;
+      if (l == kMergeAfterLayer && !a.exact) {
         // ---- token merge of x and the normalised state (ops.ts:629-661) ----
         for (int t = cta; t < T1; t += G) {
           const int b = find_req(meta->tgt_off, batch, t);
@@ -837,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         for (int i = 0; i < 8; ++i) t[h][i] = 0.f;
         for (int p = 0; p < len; ++p) {
           float v[8];
-          unpack8(__ldcg(reinterpret_cast<const uint4*>(a.nm + (base + p) * kHidden + c)), v);
+          unpack8(__ldcg(reinterpret_cast<const uint4*>((a.exact ? a.nrm : a.nm) + (base + p) * kHidden + c)), v);
 #pragma unroll
           for (int i = 0; i < 8; ++i) t[h][i] = __fadd_rn(t[h][i], v[i]);
         }

@@ -146,13 +146,14 @@ __global__ void decode_kernel(int fmt, const uint8_t* __restrict__ src, int rows
 // model.ts:226-233 with contextualMergedLength (model.ts:30-32). Lengths are
 // clamped to [1, seq] so a bad device-side input cannot index out of bounds
 // (the host API rejects such inputs before they get here).
-__global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const uint32_t* run_batch, Meta* meta) {
+__global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const uint32_t* run_batch, Meta* meta,
+                            int exact) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   if (run_batch) {
     const int rb = (int)*run_batch;
     batch = rb < 1 ? 1 : (rb > batch ? batch : rb);
   }
-  const int mseq = max(1, (int)ceil((double)seq * 0.64));
+  const int mseq = exact ? seq : max(1, (int)ceil((double)seq * 0.64));
   meta->batch = batch;
   meta->seq = seq;
   meta->merged_seq = mseq;
@@ -160,7 +161,7 @@ __global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const u
   for (int b = 0; b < batch; ++b) {
     int l = (int)lengths[b];
     l = l < 1 ? 1 : (l > seq ? seq : l);
-    int t = max(1, (int)ceil((double)l * 0.64));
+    int t = exact ? l : max(1, (int)ceil((double)l * 0.64));
     t = t < mseq ? t : mseq;
     meta->src_len[b] = l;
     meta->tgt_len[b] = t;
@@ -170,8 +171,8 @@ __global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const u
     meta->samp_off[1][b] = s1;
     o0 += l;
     o1 += t;
-    if (l > kSampleThreshold) s0 += (l + kSampleStride - 1) / kSampleStride;
-    if (t > kSampleThreshold) s1 += (t + kSampleStride - 1) / kSampleStride;
+    if (!exact && l > kSampleThreshold) s0 += (l + kSampleStride - 1) / kSampleStride;
+    if (!exact && t > kSampleThreshold) s1 += (t + kSampleStride - 1) / kSampleStride;
   }
   meta->src_off[batch] = o0;
   meta->tgt_off[batch] = o1;
@@ -179,6 +180,7 @@ __global__ void meta_kernel(const uint32_t* lengths, int batch, int seq, const u
   meta->samp_off[1][batch] = s1;
   meta->t0 = o0;
   meta->t1 = o1;
+  meta->exact = exact;
 }
 
 // ops.ts:680-725: Q6_K row gather + decode, 8 columns per thread, 1 token per
@@ -424,8 +426,8 @@ cudaError_t launch_decode(int fmt, const uint8_t* src, int rows, int k, __half* 
 }
 
 cudaError_t launch_meta(const uint32_t* lengths, int batch, int seq, const uint32_t* run_batch, Meta* meta,
-                        cudaStream_t s) {
-  meta_kernel<<<1, 32, 0, s>>>(lengths, batch, seq, run_batch, meta);
+                        cudaStream_t s, int exact) {
+  meta_kernel<<<1, 32, 0, s>>>(lengths, batch, seq, run_batch, meta, exact);
   return cudaGetLastError();
 }
 

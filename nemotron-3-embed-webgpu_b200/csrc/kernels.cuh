@@ -21,6 +21,9 @@ struct Meta {
   // Rows of the compact sampled K/V buffer per request and phase (requests
   // whose valid length exceeds 2048 keep every third key, ops.ts:258-269).
   int samp_off[2][kMaxBatch + 1];
+  // Exact-attention plans: no layer-4 merge (t1 = t0, tgt = src) and no
+  // stride-3 key sampling.
+  int exact;
 };
 
 constexpr int kSampleThreshold = 2048;
@@ -37,7 +40,7 @@ cudaError_t launch_decode(int fmt, const uint8_t* src, int rows, int k, __half* 
 // model.ts:226-233 on the device: lengths -> Meta. `batch` is the capacity;
 // when run_batch is non-null the run uses min(*run_batch, batch) requests.
 cudaError_t launch_meta(const uint32_t* lengths, int batch, int seq, const uint32_t* run_batch, Meta* meta,
-                        cudaStream_t s);
+                        cudaStream_t s, int exact = 0);
 
 // ops.ts:680-725. ids: [batch x seq] padded rows; output packed rows.
 cudaError_t launch_embedding(const uint32_t* ids, const uint8_t* table, int vocab, const Meta* meta,
@@ -185,6 +188,7 @@ struct FwdArgs {
   float* out;               // [batch x 2048]
   int n_layers;
   int chunk_max;
+  int exact;                // no merge, pool over the unmerged rows
 };
 
 size_t forward_smem_bytes(int chunk_max, int max_slots, int max_segs, int n_layers);

@@ -216,6 +216,7 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   a.out = p.out;
   a.n_layers = L;
   a.chunk_max = chunk_max;
+  a.exact = p.exact ? 1 : 0;
   // X operands by TMA; the small-T maps (box 64 x 16) exist because tmax0 <= 16.
   a.xmap[0] = p.xmap_norm[0];
   a.xmap[1] = p.xmap_norm[1];
@@ -262,7 +263,7 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
   };
   const int* t0 = &p.meta->t0;
   const int* t1 = &p.meta->t1;
-  NEMO_LAUNCH(launch_meta(p.lengths, p.cap_batch, p.seq, p.lengths + p.cap_batch, p.meta, s));
+  NEMO_LAUNCH(launch_meta(p.lengths, p.cap_batch, p.seq, p.lengths + p.cap_batch, p.meta, s, p.exact ? 1 : 0));
   Meta host_meta;
   if (dump) {
     NEMO_CUDA_TRY(cudaMemcpyAsync(&host_meta, p.meta, sizeof(Meta), cudaMemcpyDeviceToHost, s));
@@ -279,8 +280,8 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
   NEMO_LAUNCH(launch_embedding(p.ids, dm.embd, dm.vocab, p.meta, p.tmax0, p.x, s));
   NEMO_LAUNCH(launch_residual_rmsnorm(p.x, nullptr, dm.attn_norm[0], p.norm, t0, p.tmax0, s));
   for (int l = 0; l < n_layers; ++l) {
-    const bool merged = l >= kMergeAfterLayer;
-    if (l == kMergeAfterLayer) {
+    const bool merged = !p.exact && l >= kMergeAfterLayer;
+    if (l == kMergeAfterLayer && !p.exact) {
       stage(1);
       NEMO_LAUNCH(launch_merge(p.x, p.norm, p.meta, p.tmax1, p.xm, p.nm, s));
     }
@@ -373,7 +374,7 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     }
   }
   stage(10);
-  NEMO_LAUNCH(launch_mean_pool(p.nm, p.meta, p.cap_batch, p.out, s));
+  NEMO_LAUNCH(launch_mean_pool(p.exact ? p.norm : p.nm, p.meta, p.cap_batch, p.out, s));
   stage(-1);
   return kOk;
 }
@@ -418,12 +419,13 @@ int capture(DevicePlan& p, int n_layers, bool host_io, cudaGraphExec_t* out) {
   return kOk;
 }
 
-int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, DevicePlan& p) {
+int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, bool exact, DevicePlan& p) {
+  p.exact = exact;
   p.device = dm->device;
   p.dm = dm;
   p.cap_batch = cap_batch;
   p.seq = seq;
-  p.mseq = (int)std::max(1.0, ceil(seq * 0.64));
+  p.mseq = exact ? seq : (int)std::max(1.0, ceil(seq * 0.64));
   p.tmax0 = cap_batch * seq;
   p.tmax1 = cap_batch * p.mseq;
   p.rows0 = round_up(p.tmax0, kGemmTileM);
@@ -459,8 +461,8 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, D
       make_tmap_f16(&p.map_ffn, p.ffn, kInter, r0, 64, kGemmTileM))
     return kErrCuda;
   // Attention: compact sampled K/V only when a phase can exceed 2048 keys.
-  p.gather[0] = p.seq > kSampleThreshold;
-  p.gather[1] = p.mseq > kSampleThreshold;
+  p.gather[0] = !exact && p.seq > kSampleThreshold;
+  p.gather[1] = !exact && p.mseq > kSampleThreshold;
   p.rows_c = (p.gather[0] || p.gather[1]) ? p.tmax0 / kSampleStride + cap_batch + 1 : kGemmTileM;
   if (plan_alloc(p, &p.kc, (size_t)p.rows_c * kKVWidth * 2) || plan_alloc(p, &p.vc, (size_t)p.rows_c * kKVWidth * 2))
     return kErrCuda;
@@ -526,7 +528,7 @@ void rope_table_host(int sequence, float* table) {
     }
 }
 
-int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out) {
+int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, uint32_t flags, nemo_plan** out) {
   if (!m || !out) {
     set_error("nemo_plan_create: null argument");
     return kErrArgs;
@@ -544,9 +546,10 @@ int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out) {
   plan->model = m;
   plan->batch = (int)batch;
   plan->seq = (int)seq;
+  plan->exact = (flags & 1u) != 0;
   for (auto& dm : m->devs) {
     auto dp = std::make_unique<DevicePlan>();
-    int rc = create_device_plan(m, dm.get(), (int)batch, (int)seq, *dp);
+    int rc = create_device_plan(m, dm.get(), (int)batch, (int)seq, plan->exact, *dp);
     plan->devs.push_back(std::move(dp));
     if (rc) {
       for (auto& d : plan->devs) free_device_plan(*d);
@@ -556,7 +559,7 @@ int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, nemo_plan** out) {
   }
   // Multi-device plans of one request: from hp_min tokens on (default 5000,
   // NEMO_HEAD_PARALLEL_MIN overrides) the request runs head-parallel.
-  if (plan->devs.size() >= 2 && batch == 1) {
+  if (plan->devs.size() >= 2 && batch == 1 && !plan->exact) {
     const char* env = getenv("NEMO_HEAD_PARALLEL_MIN");
     plan->hp_min = env ? std::max(1, atoi(env)) : 5000;
     if ((int)seq >= plan->hp_min) {

@@ -98,6 +98,7 @@ struct DevicePlan {
   __half *kc = nullptr, *vc = nullptr;
   int rows_c = 0;
   bool gather[2] = {false, false};
+  bool exact = false;  // exact-attention plan: no token merge, no key sampling
   int splits[kMaxLayers][4] = {};
   int rstages[kMaxLayers][4] = {};
   // Persistent single-launch forward (k_forward.cu) when the plan's worst case
@@ -145,4 +146,5 @@ struct nemo_plan {
   // head-parallel over all devices (NCCL); shorter ones run on one device.
   nemo::HeadPar* hp = nullptr;
   int hp_min = 0;
+  bool exact = false;  // NEMO_PLAN_EXACT_ATTENTION
 };

@@ -20,6 +20,7 @@ import os
 import numpy as np
 
 HIDDEN = 2048
+EXACT_ATTENTION = 1  # NEMO_PLAN_EXACT_ATTENTION: no token merge, no key sampling
 NUM_STAGES = 12
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "libnemo_b200.so")
@@ -55,6 +56,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_model_destroy": (None, [P]),
         "nemo_model_info_get": (I, [P, ctypes.POINTER(ModelInfo)]),
         "nemo_plan_create": (I, [P, U32, U32, ctypes.POINTER(P)]),
+        "nemo_plan_create_ex": (I, [P, U32, U32, U32, ctypes.POINTER(P)]),
         "nemo_plan_run": (I, [P, P, S, P, S, P]),
         "nemo_plan_run_device": (I, [P, P, P, P]),
         "nemo_plan_stream": (P, [P]),
@@ -108,13 +110,15 @@ def merged_length(sequence: int) -> int:
 class NemotronExecutionPlan:
     """One (batch, sequence) plan: buffers + captured CUDA graphs on every device."""
 
-    def __init__(self, model: "NemotronB200Model", batch: int, sequence: int):
+    def __init__(self, model: "NemotronB200Model", batch: int, sequence: int, exact: bool = False):
         self.model = model
         self.batch = batch
         self.input_sequence = sequence
-        self.sequence = merged_length(sequence)
+        self.exact = exact
+        self.sequence = sequence if exact else merged_length(sequence)
         h = ctypes.c_void_p()
-        check(load_library().nemo_plan_create(model._h, batch, sequence, ctypes.byref(h)))
+        check(load_library().nemo_plan_create_ex(model._h, batch, sequence, EXACT_ATTENTION if exact else 0,
+                                                 ctypes.byref(h)))
         self._h = h
 
     def _inputs(self, ids, lengths):
@@ -218,8 +222,10 @@ class NemotronB200Model:
         check(load_library().nemo_model_info_get(self._h, ctypes.byref(i)))
         return i
 
-    def create_plan(self, batch: int, sequence: int) -> NemotronExecutionPlan:
-        plan = NemotronExecutionPlan(self, batch, sequence)
+    def create_plan(self, batch: int, sequence: int, exact: bool = False) -> NemotronExecutionPlan:
+        """EmbeddingRuntime.createPlan; exact=True drops the token merge and the
+        stride-3 key sampling (a build-specific mode, not the reference's)."""
+        plan = NemotronExecutionPlan(self, batch, sequence, exact)
         self.plans.append(plan)
         return plan
 

@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
         L.orc_model_weights_f16.argtypes = [P, ctypes.c_int, ctypes.c_int, P]
         L.orc_forward.argtypes = [P, ctypes.c_int, ctypes.c_int, P, P, P, P, P, P, ctypes.c_char_p,
                                   ctypes.c_size_t]
+        L.orc_forward_ex.argtypes = [P, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P, P, P, P,
+                                     ctypes.c_char_p, ctypes.c_size_t]
         L.orc_embedding.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P]
         L.orc_residual_rmsnorm.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.orc_matmul_f16.argtypes = [P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P]
@@ -300,7 +302,8 @@ class OracleModel:
         t = self.tensors["token_embd.weight"]
         return self._buf[t.byte_offset:t.byte_offset + t.byte_length]
 
-    def forward(self, batch: int, sequence: int, ids: np.ndarray, lengths: np.ndarray, dumps: bool = False):
+    def forward(self, batch: int, sequence: int, ids: np.ndarray, lengths: np.ndarray, dumps: bool = False,
+                exact: bool = False):
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
         lengths = np.ascontiguousarray(lengths, dtype=np.uint32)
         if ids.size != batch * sequence:
@@ -312,8 +315,8 @@ class OracleModel:
             xd = np.zeros((self.n_layers, batch * sequence, HIDDEN), dtype=np.uint16)
             nd = np.zeros_like(xd)
         err = ctypes.create_string_buffer(256)
-        rc = lib().orc_forward(self._h, batch, sequence, _p(ids), _p(lengths), _p(out),
-                               _p(xd) if dumps else None, _p(nd) if dumps else None, _p(tpl), err, 256)
+        rc = lib().orc_forward_ex(self._h, batch, sequence, _p(ids), _p(lengths), 1 if exact else 0, _p(out),
+                                  _p(xd) if dumps else None, _p(nd) if dumps else None, _p(tpl), err, 256)
         if rc:
             raise ValueError(err.value.decode())
         if dumps:

@@ -445,10 +445,15 @@ void orc_rope(const uint16_t* qkv, const int* positions, int tokens, const float
 // weights); output f16.
 void orc_attention(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, const int* offsets,
                    const uint32_t* lengths, int batch, uint16_t* out) {
+  orc_attention_ex(q, k, qkv, offsets, lengths, batch, 1, out);
+}
+
+void orc_attention_ex(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, const int* offsets,
+                      const uint32_t* lengths, int batch, int sample, uint16_t* out) {
   for (int b = 0; b < batch; ++b) {
     const int len = (int)lengths[b];
     const int base = offsets[b];
-    const int stride = len > 2048 ? 3 : 1;
+    const int stride = sample && len > 2048 ? 3 : 1;
     const int nkeys = (len + stride - 1) / stride;
 #pragma omp parallel
     {
@@ -642,6 +647,12 @@ int orc_model_weights_f16(const orc_model* model, int layer, int which, uint16_t
 int orc_forward(const orc_model* m, int batch, int sequence, const uint32_t* ids,
                 const uint32_t* lengths, float* out, uint16_t* x_dump, uint16_t* norm_dump,
                 int* tokens_per_layer, char* err, size_t errlen) {
+  return orc_forward_ex(m, batch, sequence, ids, lengths, 0, out, x_dump, norm_dump, tokens_per_layer, err, errlen);
+}
+
+int orc_forward_ex(const orc_model* m, int batch, int sequence, const uint32_t* ids,
+                   const uint32_t* lengths, int exact, float* out, uint16_t* x_dump, uint16_t* norm_dump,
+                   int* tokens_per_layer, char* err, size_t errlen) {
   if (!m || batch < 1 || sequence < 1) {
     set_err(err, errlen, "invalid plan shape");
     return -1;
@@ -663,7 +674,7 @@ int orc_forward(const orc_model* m, int batch, int sequence, const uint32_t* ids
   for (int b = 0; b < batch; ++b) {
     const uint32_t src = lengths[b] < (uint32_t)sequence ? lengths[b] : (uint32_t)sequence;
     const uint32_t ml = orc_merged_length(src);
-    tgt[b] = ml < merged_seq ? ml : merged_seq;
+    tgt[b] = exact ? lengths[b] : (ml < merged_seq ? ml : merged_seq);
     off0[b + 1] = off0[b] + (int)lengths[b];
     off1[b + 1] = off1[b] + (int)tgt[b];
   }
@@ -693,7 +704,7 @@ int orc_forward(const orc_model* m, int batch, int sequence, const uint32_t* ids
   const uint32_t* layer_len = lengths;
   const int* positions = pos0.data();
   for (int l = 0; l < m->n_layers; ++l) {
-    if (l == kMergeAfterLayer) {  // model.ts:157, merge both x and normalized
+    if (l == kMergeAfterLayer && !exact) {  // model.ts:157, merge both x and normalized
       std::vector<uint16_t> xm((size_t)t1 * kHidden), nm((size_t)t1 * kHidden);
       orc_token_merge(x.data(), off0.data(), lengths, off1.data(), tgt.data(), batch, xm.data());
       orc_token_merge(norm.data(), off0.data(), lengths, off1.data(), tgt.data(), batch, nm.data());
@@ -706,7 +717,7 @@ int orc_forward(const orc_model* m, int batch, int sequence, const uint32_t* ids
     }
     orc_matmul_f16(norm.data(), m->w[l][0].data(), tokens, kQKVWidth, kHidden, nullptr, qkv.data());
     orc_rope(qkv.data(), positions, tokens, rope.data(), qb.data(), kb.data());
-    orc_attention(qb.data(), kb.data(), qkv.data(), offsets, layer_len, batch, attn.data());
+    orc_attention_ex(qb.data(), kb.data(), qkv.data(), offsets, layer_len, batch, exact ? 0 : 1, attn.data());
     orc_matmul_f16(attn.data(), m->w[l][1].data(), tokens, kHidden, kQWidth, nullptr, delta.data());
     orc_residual_rmsnorm(x.data(), delta.data(), m->ffn_norm[l], norm.data(), tokens, kHidden, kEpsilon);
     orc_matmul_f16(norm.data(), m->w[l][2].data(), tokens, 2 * kInter, kHidden, nullptr, gu.data());

@@ -115,6 +115,12 @@ int orc_model_weights_f16(const orc_model* model, int layer, int which, uint16_t
 int orc_forward(const orc_model* model, int batch, int sequence, const uint32_t* ids,
                 const uint32_t* lengths, float* out, uint16_t* x_dump, uint16_t* norm_dump,
                 int* tokens_per_layer, char* err, size_t errlen);
+/* Same with exact != 0: no layer-4 token merge and no stride-3 key sampling
+ * (every layer attends over every valid key of the request). Not a reference
+ * mode: the oracle of the build's exact-attention plans. */
+int orc_forward_ex(const orc_model* model, int batch, int sequence, const uint32_t* ids,
+                   const uint32_t* lengths, int exact, float* out, uint16_t* x_dump, uint16_t* norm_dump,
+                   int* tokens_per_layer, char* err, size_t errlen);
 
 /* Individual stages on packed valid tokens, for kernel-level parity tests.
  * All f16 buffers hold bit patterns. */
@@ -128,7 +134,10 @@ void orc_rope_table(int sequence, float* table);                             /* 
 void orc_rope(const uint16_t* qkv, const int* positions, int tokens, const float* table,
               uint16_t* q, uint16_t* k);                                     /* ops.ts:168-194 */
 void orc_attention(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, const int* offsets,
-                   const uint32_t* lengths, int batch, uint16_t* out);       /* ops.ts:213-362 */
+                   const uint32_t* lengths, int batch, uint16_t* out);
+/* sample = 0: every key, whatever the length. */
+void orc_attention_ex(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, const int* offsets,
+                      const uint32_t* lengths, int batch, int sample, uint16_t* out);       /* ops.ts:213-362 */
 void orc_swiglu(const uint16_t* gate_up, int rows, uint16_t* out);           /* ops.ts:74-89 */
 void orc_token_merge(const uint16_t* in, const int* src_offsets, const uint32_t* src_lengths,
                      const int* dst_offsets, const uint32_t* dst_lengths, int batch,

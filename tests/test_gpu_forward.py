@@ -210,3 +210,52 @@ def test_long_context_sampling():
     finally:
         gpu.destroy()
         orc.close()
+
+
+def exact_compare(gpu, orc, lengths, seed):
+    reqs = synth.make_requests(seed, lengths, vocab=orc.vocab)
+    ids, lens, seq = synth.pad_batch(reqs)
+    plan = gpu.create_plan(len(lengths), seq, exact=True)
+    try:
+        got, gdump = plan.run_debug(ids, lens)
+        fast = plan.run_array(ids, lens).copy()
+    finally:
+        plan.destroy()
+    want, odump = orc.forward(len(lengths), seq, ids, lens, dumps=True, exact=True)
+    for l, ((gx, gn), (ox, on)) in enumerate(zip(gdump, odump)):
+        assert gx.shape == ox.shape == (sum(lengths), 2048), l  # no merge: every layer keeps all tokens
+        assert rel_err(f16_of_bits(gx), f16_of_bits(ox)) <= LAYER_TOL, l
+        assert rel_err(f16_of_bits(gn), f16_of_bits(on)) <= LAYER_TOL, l
+    for b in range(len(lengths)):
+        assert cosine(got[b], want[b]) >= COS_TOL, b
+        assert cosine(fast[b], want[b]) >= COS_TOL, b
+        assert abs(np.linalg.norm(fast[b]) - 1) < 1e-3
+    return want, ids, lens, seq
+
+
+@pytest.mark.parametrize("lengths", [[15], [300, 170]])
+def test_exact_attention_plans(models, lengths):
+    """NEMO_PLAN_EXACT_ATTENTION: no layer-4 merge, no key sampling, on the
+    single-launch (<= 16 tokens) and batched paths, against the oracle's
+    exact forward; the mode really differs from the reference semantics."""
+    flavour, gpu, orc = models
+    if flavour != "kquant" and lengths != [15]:
+        pytest.skip("one flavour is enough at this size")
+    want, ids, lens, seq = exact_compare(gpu, orc, lengths, seed=31)
+    merged = orc.forward(len(lengths), seq, ids, lens)
+    assert min(cosine(want[b], merged[b]) for b in range(len(lengths))) < 0.99999
+
+
+def test_exact_attention_long_request():
+    """A 2100-token request attends over all 2100 keys in exact mode (the
+    reference keeps every third key above 2048)."""
+    path = synth.cached_model_pack(2, "kquant", 5)
+    with open(path, "rb") as f:
+        data = f.read()
+    gpu = NemotronB200Model(data)
+    orc = oracle.OracleModel(data)
+    try:
+        exact_compare(gpu, orc, [2100, 40], seed=13)
+    finally:
+        gpu.destroy()
+        orc.close()
