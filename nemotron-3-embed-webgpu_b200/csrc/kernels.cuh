@@ -145,6 +145,15 @@ size_t skinny_smem_bytes(int np, int slabs_max, int chunk_max, int rstages);
 // np = tokens padded to 16, 32 or 64; map_x box 64 x np.
 cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np, int tiles, cudaStream_t s);
 
+// --- dequant-fused batched projection GEMM (k_gemm_q.cu) --------------------
+// Y[M x 128 * n_tiles] = X . W^T with W decoded from the tile-slab image in
+// shared memory; map_x box 64 x 128 (128B swizzle). mode kSkinnyPlain stores
+// f16 rows (ldy wide); kSkinnySwiglu applies SwiGLU to each tile's interleaved
+// gate/up rows and stores 64 columns per tile ([M x 6144]).
+cudaError_t launch_gemm_q(const CUtensorMap* map_x, const uint8_t* packed, const SkinnyTile* tiles, int n_tiles,
+                          int slabs, int chunk_max, int mode, __half* y, int ldy, const int* d_rows, int max_rows,
+                          uint32_t* err, cudaStream_t s);
+
 // --- persistent single-launch forward for <= kFwdNP tokens (k_forward.cu) ---
 constexpr int kFwdNP = 16;        // token rows per projection (padded)
 constexpr int kFwdMaxTiles = 96;  // 128-row tiles of the widest projection (gate/up)

@@ -320,13 +320,23 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
       NEMO_LAUNCH(launch_skinny(xmap, a, np, P.tiles, s));
       return kOk;
     };
+    // Batched token counts: dequant-fused tcgen05 GEMM over the packed weights.
+    auto gemm_q = [&](int which, const CUtensorMap* xmap, int mode, __half* out, int ldo) -> int {
+      const Projection& P = pr[which];
+      NEMO_LAUNCH(launch_gemm_q(xmap, P.packed, P.d_tiles, P.tiles, P.slabs, P.chunk_max, mode, out, ldo, rows, maxr,
+                                p.err, s));
+      return kOk;
+    };
     stage(2);
     if (np) {
       if (int rc = skinny(kProjQKV, &p.xmap_norm[ph], kSkinnyRope, p.qkv, kQKVWidth)) return rc;
       stage(3);
     } else {
-      NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth,
-                                 kHidden, kBnChoices[p.bn[l][0]], p.err, s));
+      if (p.batched_f16)
+        NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth,
+                                   kHidden, kBnChoices[p.bn[l][0]], p.err, s));
+      else if (int rc = gemm_q(kProjQKV, mapN, kSkinnyPlain, p.qkv, kQKVWidth))
+        return rc;
       stage(3);
       NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
     }
@@ -335,9 +345,11 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     stage(4);
     if (np) {
       if (int rc = skinny(kProjO, &p.xmap_attn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
-    } else {
+    } else if (p.batched_f16) {
       NEMO_LAUNCH(launch_gemm_tc(&p.map_attn, &pr[kProjO].map[p.bn[l][1]], p.delta, kHidden, rows, maxr, kHidden,
                                  kQWidth, kBnChoices[p.bn[l][1]], p.err, s));
+    } else if (int rc = gemm_q(kProjO, &p.map_attn, kSkinnyPlain, p.delta, kHidden)) {
+      return rc;
     }
     stage(5);
     NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, dm.ffn_norm[l], N, rows, maxr, s));
@@ -345,18 +357,24 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     if (np) {
       if (int rc = skinny(kProjGateUp, &p.xmap_norm[ph], kSkinnySwiglu, p.ffn, kInter)) return rc;
       stage(7);
-    } else {
+    } else if (p.batched_f16) {
       NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjGateUp].map[p.bn[l][2]], p.gu, 2 * kInter, rows, maxr, 2 * kInter,
                                  kHidden, kBnChoices[p.bn[l][2]], p.err, s));
       stage(7);
       NEMO_LAUNCH(launch_swiglu(p.gu, rows, maxr, p.ffn, s));
+    } else {
+      // SwiGLU fused into the epilogue (tiles interleave 64 gate + 64 up rows)
+      if (int rc = gemm_q(kProjGateUp, mapN, kSkinnySwiglu, p.ffn, kInter)) return rc;
+      stage(7);
     }
     stage(8);
     if (np) {
       if (int rc = skinny(kProjDown, &p.xmap_ffn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
-    } else {
+    } else if (p.batched_f16) {
       NEMO_LAUNCH(launch_gemm_tc(&p.map_ffn, &pr[kProjDown].map[p.bn[l][3]], p.delta, kHidden, rows, maxr, kHidden,
                                  kInter, kBnChoices[p.bn[l][3]], p.err, s));
+    } else if (int rc = gemm_q(kProjDown, &p.map_ffn, kSkinnyPlain, p.delta, kHidden)) {
+      return rc;
     }
     stage(9);
     const float* next = l + 1 < n_layers ? dm.attn_norm[l + 1] : dm.output_norm;
@@ -421,6 +439,10 @@ int capture(DevicePlan& p, int n_layers, bool host_io, cudaGraphExec_t* out) {
 
 int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, bool exact, DevicePlan& p) {
   p.exact = exact;
+  {
+    const char* env = getenv("NEMO_BATCHED");
+    p.batched_f16 = !(env && strcmp(env, "fused") == 0);
+  }
   p.device = dm->device;
   p.dm = dm;
   p.cap_batch = cap_batch;

@@ -99,6 +99,11 @@ struct DevicePlan {
   int rows_c = 0;
   bool gather[2] = {false, false};
   bool exact = false;  // exact-attention plan: no token merge, no key sampling
+  // Batched projections (> 64 tokens): tcgen05 GEMM over the f16 weights
+  // decoded at load (default: measured faster at every batched size here), or
+  // the dequant-fused tcgen05 GEMM over the packed blocks (NEMO_BATCHED=fused
+  // at plan creation).
+  bool batched_f16 = true;
   int splits[kMaxLayers][4] = {};
   int rstages[kMaxLayers][4] = {};
   // Persistent single-launch forward (k_forward.cu) when the plan's worst case

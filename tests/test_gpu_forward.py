@@ -144,6 +144,37 @@ def test_medium_sequence(models):
     compare(gpu, orc, [300, 170], seed=3)
 
 
+@pytest.mark.parametrize("lengths", [[150, 97, 64], [700] * 3, [520, 9]])
+def test_batched_dequant_fused_vs_f16_weights(models, lengths, monkeypatch):
+    """NEMO_BATCHED=fused: batched plans (> 64 tokens) decode the packed blocks
+    to f16 in shared memory inside the tcgen05 GEMM (128, 256 or 512 tokens per
+    CTA, by size; gate/up with SwiGLU in its epilogue). The default path
+    multiplies the same effective f16 weights, decoded once at load, with the
+    plain tcgen05 GEMM and a separate SwiGLU kernel. Same operands and f32
+    accumulation: the embeddings agree to rounding noise, and both match the
+    oracle."""
+    flavour, gpu, orc = models
+    if flavour != "kquant" and lengths != [150, 97, 64]:
+        pytest.skip("one flavour is enough at this size")
+    reqs = synth.make_requests(11, lengths, vocab=orc.vocab)
+    ids, lens, seq = synth.pad_batch(reqs)
+    with monkeypatch.context() as m:
+        m.setenv("NEMO_BATCHED", "fused")
+        plan = gpu.create_plan(len(lengths), seq)
+    assert not is_fused(plan)
+    got = np.stack(plan.run(ids, lens))
+    again = np.stack(plan.run(ids, lens))
+    plan.destroy()
+    assert np.array_equal(got, again)
+    f16_plan = gpu.create_plan(len(lengths), seq)
+    ref = np.stack(f16_plan.run(ids, lens))
+    f16_plan.destroy()
+    want = orc.forward(len(lengths), seq, ids, lens)
+    for b in range(len(lengths)):
+        assert cosine(got[b], ref[b]) >= 0.99999, b
+        assert cosine(got[b], want[b]) >= COS_TOL, b
+
+
 def test_plan_reuse_is_deterministic(models):
     _, gpu, orc = models
     reqs = synth.make_requests(5, [20, 9], vocab=orc.vocab)
