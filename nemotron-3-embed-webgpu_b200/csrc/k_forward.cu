@@ -72,13 +72,14 @@ __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* er
   }
 }
 
+
+__device__ __forceinline__ void pw_sync() { dev::named_barrier(1, 128); }
+
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-
-__device__ __forceinline__ void pw_sync() { dev::named_barrier(1, 128); }
 
 // 16-byte asynchronous global -> shared copy through L2 (many in flight per
 // thread without registers), and the wait for all of this thread's copies.
@@ -575,8 +576,10 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     auto set_quiet = [&](bool on) {
       if (pt == 0) *reinterpret_cast<volatile int*>(&sh->quiet) = on ? 1 : 0;
     };
+    // Only CTAs that hold items quiet their decoders: the others keep the
+    // weight rings filling through the small phases.
     auto norm_phase = [&](__half* x, int rpi, const float* w, __half* out, int T) {
-      set_quiet(true);
+      if (cta < T) set_quiet(true);
       for (int t = cta; t < T; t += G) norm_row(x, rpi, w, out, t);
       set_quiet(false);
     };
@@ -725,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         float* linv = ps + 8 * NP;                     // [8]
         const int* off = merged ? meta->tgt_off : meta->src_off;
         constexpr int kQG = 8, kGroups = (NP + kQG - 1) / kQG;
-        set_quiet(true);
+        if (cta < batch * kQHeads * kGroups) set_quiet(true);
         for (int item = cta; item < batch * kQHeads * kGroups; item += G) {
           const int b = item / (kQHeads * kGroups), rem = item % (kQHeads * kGroups);
           const int h = rem / kGroups, g = rem % kGroups, kvh = h / (kQHeads / kKVHeads);
@@ -763,44 +766,51 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
               for (int e = 0; e < 8; ++e) dsts[k][e] = f[e];
             }
           pw_sync();
-          const float scale = 0.08838834764831845f;
-          for (int e = pt; e < nq * len; e += 128) {
-            const int i = e / len, j = e - i * len;
-            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+          {
+            // thread = (query i, key j): kQG x NP = 128 scores; each query
+            // row's softmax runs across its 16 lanes by shuffles
+            static_assert(kQG * NP == 128, "one score per phase thread");
+            const float scale = 0.08838834764831845f;
+            const int i = pt >> 4, j = pt & 15;
+            const bool valid = i < nq && j < len;
+            float sc = -INFINITY;
+            if (valid) {
+              float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
-            for (int dd = 0; dd < kHeadDim; dd += 4) {
-              const int d = (dd + 4 * j) & (kHeadDim - 1);
-              const float4 q4 = *reinterpret_cast<const float4*>(qs + i * kHeadDim + d);
-              const float4 k4 = *reinterpret_cast<const float4*>(ks + j * kHeadDim + d);
-              s4[0] = fmaf(q4.x, k4.x, s4[0]);
-              s4[1] = fmaf(q4.y, k4.y, s4[1]);
-              s4[2] = fmaf(q4.z, k4.z, s4[2]);
-              s4[3] = fmaf(q4.w, k4.w, s4[3]);
+              for (int dd = 0; dd < kHeadDim; dd += 4) {
+                const int d = (dd + 4 * j) & (kHeadDim - 1);
+                const float4 q4 = *reinterpret_cast<const float4*>(qs + i * kHeadDim + d);
+                const float4 k4 = *reinterpret_cast<const float4*>(ks + j * kHeadDim + d);
+                s4[0] = fmaf(q4.x, k4.x, s4[0]);
+                s4[1] = fmaf(q4.y, k4.y, s4[1]);
+                s4[2] = fmaf(q4.z, k4.z, s4[2]);
+                s4[3] = fmaf(q4.w, k4.w, s4[3]);
+              }
+              const int pos = q0 + i;
+              const float temp = pos >= 16384 ? logf(floorf((float)pos / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
+              sc = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale * temp;
             }
-            const int pos = q0 + i;
-            const float temp = pos >= 16384 ? logf(floorf((float)pos / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
-            ps[i * NP + j] = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * scale * temp;
-          }
-          pw_sync();
-          if (pt < nq) {  // softmax of query row pt
-            float m = -INFINITY;
-            for (int j = 0; j < len; ++j) m = fmaxf(m, ps[pt * NP + j]);
-            float l = 0.f;
-            for (int j = 0; j < len; ++j) {
-              const float p = expf(ps[pt * NP + j] - m);
-              ps[pt * NP + j] = p;
-              l += p;
-            }
-            linv[pt] = 1.0f / l;
+            float m = sc;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float p = valid ? expf(sc - m) : 0.f;
+            float lsum = p;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            ps[i * NP + j] = p;
+            if (j == 0) linv[i] = 1.0f / lsum;
           }
           pw_sync();
           float acc[kQG];
 #pragma unroll
           for (int i = 0; i < kQG; ++i) acc[i] = 0.f;
-          for (int j = 0; j < len; ++j) {
-            const float v = vs[j * kHeadDim + pt];
 #pragma unroll
-            for (int i = 0; i < kQG; ++i) acc[i] = fmaf(ps[i * NP + j], v, acc[i]);
+          for (int j = 0; j < NP; ++j) {
+            if (j < len) {
+              const float v = vs[j * kHeadDim + pt];
+#pragma unroll
+              for (int i = 0; i < kQG; ++i) acc[i] = fmaf(ps[i * NP + j], v, acc[i]);
+            }
           }
 #pragma unroll
           for (int i = 0; i < kQG; ++i)
