@@ -11,7 +11,10 @@
 //   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16 per
 //               instruction; converged warp, elected lane), tcgen05.commit
 //               frees each stage
-//   warps 2..5  epilogue: tcgen05.ld 32x32b (one row per thread), f16 store
+//   warps 2..5  epilogue: tcgen05.ld 32x32b (one row per thread), then an f16
+//               store, RoPE (QKV: Q/K pairs rotated into the attention
+//               inputs, ops.ts:168-194) or SwiGLU (gate/up: the B tile holds
+//               BN/2 gate rows then the matching BN/2 up rows, ops.ts:74-89)
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error word,
 // drains what this CTA has in flight and frees its TMEM before returning.
 #include <cudaTypedefs.h>
@@ -36,7 +39,7 @@ struct GemmCfg {
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, __half* y,
-                   int ldy, const int* __restrict__ d_rows, int k, uint32_t* err) {
+                   int ldy, const int* __restrict__ d_rows, int k, uint32_t* err, GemmEpi e) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const int M = *d_rows;
@@ -86,7 +89,14 @@ __global__ void __launch_bounds__(192, 1)
       if (dev::elect_one()) {
         dev::mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES);
         dev::tma_load_2d(sa, &map_a, kt * C::BK, m0, full0 + 8 * s);
-        dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
+        if (e.mode == kSkinnySwiglu) {
+          // map_b box is BN/2 rows: gate rows, then the matching up rows
+          dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, blockIdx.x * (BN / 2), full0 + 8 * s);
+          dev::tma_load_2d(sa + C::A_BYTES + (BN / 2) * 128, &map_b, kt * C::BK, kInter + blockIdx.x * (BN / 2),
+                           full0 + 8 * s);
+        } else {
+          dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
+        }
       }
       __syncwarp();
       ++issued;
@@ -124,10 +134,75 @@ __global__ void __launch_bounds__(192, 1)
     const int row = m0 + quarter * 32 + lane;
     if (__all_sync(0xffffffffu, dev::mbar_wait(accum, 0, err))) {  // warp-uniform: tcgen05.ld is collective
       dev::tc_fence_after();
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16);
+      if (e.mode == kSkinnySwiglu) {
+        // out[row][g] = f16(silu(f16 gate) * f16 up) for the tile's BN/2 outputs
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          dev::tmem_ld_32x32b_x32(tbase + c, g);
+          dev::tmem_ld_32x32b_x32(tbase + BN / 2 + c, u);
+          dev::tc_wait_ld();
+          if (row < M) {
+            uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + blockIdx.x * (BN / 2) + c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float o[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float gh = __half2float(__float2half_rn(__uint_as_float(g[v * 8 + j])));
+                const float uh = __half2float(__float2half_rn(__uint_as_float(u[v * 8 + j])));
+                o[j] = __fmul_rn(__fdiv_rn(gh, __fadd_rn(1.0f, expf(-gh))), uh);
+              }
+              uint4 w;
+              __half2* h = reinterpret_cast<__half2*>(&w);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+              dst[v] = w;
+            }
+          }
+        }
+      } else {
+      // RoPE: position of this token row within its request (ops.ts:188)
+      int pos = 0;
+      if (e.mode == kSkinnyRope && row < M) {
+        const int* off = e.merged ? e.meta->tgt_off : e.meta->src_off;
+        int b = 0;
+        while (b + 1 < e.meta->batch && row >= off[b + 1]) ++b;
+        pos = row - off[b];
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
+          uint32_t r[32];
+          dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
+          dev::tc_wait_ld();
+          if (row < M) {
+            // (even, odd) column pairs rotated by the table row of pos, as the
+            // f16-stored QKV would be (k_misc.cu rope_kernel)
+            const float* cs = e.rope + ((size_t)pos * 64 + ((col0 & 127) >> 1)) * 2;
+            uint32_t o[16];
+#pragma unroll
+            for (int p = 0; p < 16; ++p) {
+              const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
+              const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
+              const float2 t = *reinterpret_cast<const float2*>(cs + 2 * p);
+              const float first = __fsub_rn(__fmul_rn(even, t.x), __fmul_rn(odd, t.y));
+              const float second = __fadd_rn(__fmul_rn(even, t.y), __fmul_rn(odd, t.x));
+              __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
+              o[p] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            __half* dst = col0 < kQWidth ? e.q + (size_t)row * kQWidth + col0
+                                         : e.k + (size_t)row * kKVWidth + (col0 - kQWidth);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+          }
+          continue;
+        }
         uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + c * 32, r);
+        dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
         dev::tc_wait_ld();
         if (row < M) {
           uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + n0 + c * 32);
@@ -142,6 +217,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+      }
     }
   }
   dev::tc_fence_before();
@@ -154,7 +230,7 @@ __global__ void __launch_bounds__(192, 1)
 
 template <int BN>
 cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
-                      int max_rows, int n, int k, uint32_t* err, cudaStream_t s) {
+                      int max_rows, int n, int k, uint32_t* err, const GemmEpi& ep, cudaStream_t s) {
   using C = GemmCfg<BN>;
   static bool configured[64] = {};
   int dev = 0;
@@ -167,7 +243,7 @@ cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, i
     configured[dev] = true;
   }
   dim3 grid(n / BN, (max_rows + C::BM - 1) / C::BM);
-  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, err);
+  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, err, ep);
   return cudaGetLastError();
 }
 
@@ -185,15 +261,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-cudaError_t launch_gemm_tc(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
-                           int max_rows, int n, int k, int bn, uint32_t* err, cudaStream_t s) {
+cudaError_t launch_gemm_tc_epi(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
+                               int max_rows, int n, int k, int bn, const GemmEpi& ep, uint32_t* err, cudaStream_t s) {
   if (k % 64 != 0 || n % bn != 0) return cudaErrorInvalidValue;
+  if (ep.mode == kSkinnySwiglu && (bn < 128 || n != 2 * kInter)) return cudaErrorInvalidValue;
+  if (ep.mode == kSkinnyRope && (n != kQKVWidth || !ep.meta || !ep.rope || !ep.q || !ep.k)) return cudaErrorInvalidValue;
   switch (bn) {
-    case 64: return launch_bn<64>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
-    case 128: return launch_bn<128>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
-    case 256: return launch_bn<256>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, s);
+    case 64: return launch_bn<64>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, ep, s);
+    case 128: return launch_bn<128>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, ep, s);
+    case 256: return launch_bn<256>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, ep, s);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_gemm_tc(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, int ldy, const int* d_rows,
+                           int max_rows, int n, int k, int bn, uint32_t* err, cudaStream_t s) {
+  return launch_gemm_tc_epi(ma, mb, y, ldy, d_rows, max_rows, n, k, bn, GemmEpi{}, err, s);
 }
 
 int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,

@@ -105,6 +105,23 @@ cudaError_t launch_gemm_simt(const __half* x, const __half* w, __half* y, float*
 cudaError_t launch_gemm_tc(const CUtensorMap* map_a, const CUtensorMap* map_b, __half* y, int ldy,
                            const int* d_rows, int max_rows, int n, int k, int bn, uint32_t* err,
                            cudaStream_t s);
+// Fused epilogues of the tcgen05 GEMM (mode: kSkinnyPlain, kSkinnyRope,
+// kSkinnySwiglu). RoPE (QKV, n = 5120): Q and K columns are rotated by the
+// table row of the token's position and written to q [T x 3072] and
+// k [T x 1024]; V columns go to y. SwiGLU (gate/up, n = 12288, bn >= 128):
+// map_b has a box of bn/2 rows; CTA x multiplies gate rows [x*bn/2, +bn/2) and
+// the matching up rows and writes SwiGLU to y [T x ldy] at column x*bn/2.
+struct GemmEpi {
+  int mode = 0;
+  const Meta* meta = nullptr;
+  int merged = 0;
+  const float* rope = nullptr;
+  __half* q = nullptr;
+  __half* k = nullptr;
+};
+cudaError_t launch_gemm_tc_epi(const CUtensorMap* map_a, const CUtensorMap* map_b, __half* y, int ldy,
+                               const int* d_rows, int max_rows, int n, int k, int bn, const GemmEpi& ep,
+                               uint32_t* err, cudaStream_t s);
 
 // --- fused-dequant split-K projection for T <= 64 tokens (k_skinny.cu) -----
 // Packed weights are re-tiled at load into 128-row tiles x 256-column slabs:

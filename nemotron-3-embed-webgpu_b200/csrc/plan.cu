@@ -332,13 +332,23 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
       if (int rc = skinny(kProjQKV, &p.xmap_norm[ph], kSkinnyRope, p.qkv, kQKVWidth)) return rc;
       stage(3);
     } else {
-      if (p.batched_f16)
-        NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth,
-                                   kHidden, kBnChoices[p.bn[l][0]], p.err, s));
-      else if (int rc = gemm_q(kProjQKV, mapN, kSkinnyPlain, p.qkv, kQKVWidth))
-        return rc;
-      stage(3);
-      NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
+      if (p.batched_f16) {
+        // RoPE in the GEMM epilogue: Q/K straight into the attention inputs
+        GemmEpi ep;
+        ep.mode = kSkinnyRope;
+        ep.meta = p.meta;
+        ep.merged = merged ? 1 : 0;
+        ep.rope = p.rope;
+        ep.q = p.q;
+        ep.k = p.k;
+        NEMO_LAUNCH(launch_gemm_tc_epi(mapN, &pr[kProjQKV].map[p.bn[l][0]], p.qkv, kQKVWidth, rows, maxr, kQKVWidth,
+                                       kHidden, kBnChoices[p.bn[l][0]], ep, p.err, s));
+        stage(3);
+      } else {
+        if (int rc = gemm_q(kProjQKV, mapN, kSkinnyPlain, p.qkv, kQKVWidth)) return rc;
+        stage(3);
+        NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
+      }
     }
     if (p.gather[ph]) NEMO_LAUNCH(launch_gather_sampled(p.k, p.qkv, p.meta, merged, p.rows_c, p.kc, p.vc, s));
     NEMO_LAUNCH(launch_attention_tc(p.amaps, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, p.err, s));
@@ -358,10 +368,14 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
       if (int rc = skinny(kProjGateUp, &p.xmap_norm[ph], kSkinnySwiglu, p.ffn, kInter)) return rc;
       stage(7);
     } else if (p.batched_f16) {
-      NEMO_LAUNCH(launch_gemm_tc(mapN, &pr[kProjGateUp].map[p.bn[l][2]], p.gu, 2 * kInter, rows, maxr, 2 * kInter,
-                                 kHidden, kBnChoices[p.bn[l][2]], p.err, s));
+      // SwiGLU in the GEMM epilogue: each CTA multiplies bn/2 gate rows and
+      // the matching up rows (tensor map box bn/2), so bn >= 128
+      const int bi = std::max(1, p.bn[l][2]);
+      GemmEpi ep;
+      ep.mode = kSkinnySwiglu;
+      NEMO_LAUNCH(launch_gemm_tc_epi(mapN, &pr[kProjGateUp].map[bi - 1], p.ffn, kInter, rows, maxr, 2 * kInter,
+                                     kHidden, kBnChoices[bi], ep, p.err, s));
       stage(7);
-      NEMO_LAUNCH(launch_swiglu(p.gu, rows, maxr, p.ffn, s));
     } else {
       // SwiGLU fused into the epilogue (tiles interleave 64 gate + 64 up rows)
       if (int rc = gemm_q(kProjGateUp, mapN, kSkinnySwiglu, p.ffn, kInter)) return rc;
