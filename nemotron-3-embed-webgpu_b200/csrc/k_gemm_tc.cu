@@ -5,9 +5,12 @@
 // src/webgpu/model.ts:126-134; the weights are the effective f16 values of the
 // quantised blocks, decoded once at load.
 //
-// One CTA computes a 128 x BN tile. Warp roles (192 threads):
+// Persistent: one CTA per SM walks its 128 x BN output tiles; two TMEM
+// accumulators let the epilogue of one tile overlap the MMAs of the next.
+// Warp roles (192 threads):
 //   warp 0      TMA producer: 64-wide K slabs of A (128 x 64) and B (BN x 64)
-//               into a STAGES-deep ring, 128-byte swizzled, mbarrier complete_tx
+//               into a STAGES-deep ring that runs on across tiles, 128-byte
+//               swizzled, mbarrier complete_tx
 //   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16 per
 //               instruction; converged warp, elected lane), tcgen05.commit
 //               frees each stage
@@ -18,6 +21,8 @@
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error word,
 // drains what this CTA has in flight and frees its TMEM before returning.
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "kernels.cuh"
 
@@ -32,20 +37,20 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i || MMAs of tile i + 1
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
+// Persistent: CTA c takes tiles c, c + grid, ... of the (m tile, n tile)
+// grid in n-fastest order; M (valid token rows) is read on the device.
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, __half* y,
-                   int ldy, const int* __restrict__ d_rows, int k, uint32_t* err, GemmEpi e) {
+                   int ldy, const int* __restrict__ d_rows, int k, int n_tiles, uint32_t* err, GemmEpi e) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const int M = *d_rows;
-  const int m0 = blockIdx.y * C::BM;
-  if (m0 >= M) return;  // uniform over the CTA
-  const int n0 = blockIdx.x * BN;
+  const int total = (M + C::BM - 1) / C::BM * n_tiles;
   // 1024-byte alignment of the shared-window address (the 128-byte swizzle
   // pattern repeats every 1024 bytes and the descriptors assume base offset 0).
   const uint32_t raw_s = dev::smem_u32(smem_raw);
@@ -53,8 +58,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   const uint32_t full0 = dev::smem_u32(bars);
   const uint32_t empty0 = full0 + 8 * C::STAGES;
-  const uint32_t accum = empty0 + 8 * C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 1);
+  const uint32_t tfull = empty0 + 8 * C::STAGES, tempty = tfull + 16, fin = tempty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5);
   const uint32_t sbase = dev::smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KT = k / C::BK;
@@ -66,7 +71,11 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_init(full0 + 8 * s, 1);
       dev::mbar_init(empty0 + 8 * s, 1);
     }
-    dev::mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      dev::mbar_init(tfull + 8 * b, 1);
+      dev::mbar_init(tempty + 8 * b, 128);
+    }
+    dev::mbar_init(fin, 1);
     dev::fence_mbar_init();
   }
   if (warp == 1) {
@@ -79,62 +88,86 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // Converged warp; the elected lane issues the copies.
-    int issued = 0;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % C::STAGES;
-      const uint32_t ph = (kt / C::STAGES) & 1;
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(empty0 + 8 * s, ph ^ 1, err))) break;
-      const uint32_t sa = sbase + s * C::STAGE_BYTES;
-      if (dev::elect_one()) {
-        dev::mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES);
-        dev::tma_load_2d(sa, &map_a, kt * C::BK, m0, full0 + 8 * s);
-        if (e.mode == kSkinnySwiglu) {
-          // map_b box is BN/2 rows: gate rows, then the matching up rows
-          dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, blockIdx.x * (BN / 2), full0 + 8 * s);
-          dev::tma_load_2d(sa + C::A_BYTES + (BN / 2) * 128, &map_b, kt * C::BK, kInter + blockIdx.x * (BN / 2),
-                           full0 + 8 * s);
-        } else {
-          dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
+    // Converged warp; the elected lane issues the copies. The stage ring runs
+    // on across tiles.
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const int m0 = (t / n_tiles) * C::BM, nt = t % n_tiles, n0 = nt * BN;
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % C::STAGES;
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(empty0 + 8 * s, ((it / C::STAGES) & 1) ^ 1, err))) {
+          ok = false;
+          break;
         }
+        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+        if (dev::elect_one()) {
+          dev::mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES);
+          dev::tma_load_2d(sa, &map_a, kt * C::BK, m0, full0 + 8 * s);
+          if (e.mode == kSkinnySwiglu) {
+            // map_b box is BN/2 rows: gate rows, then the matching up rows
+            dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, nt * (BN / 2), full0 + 8 * s);
+            dev::tma_load_2d(sa + C::A_BYTES + (BN / 2) * 128, &map_b, kt * C::BK, kInter + nt * (BN / 2),
+                             full0 + 8 * s);
+          } else {
+            dev::tma_load_2d(sa + C::A_BYTES, &map_b, kt * C::BK, n0, full0 + 8 * s);
+          }
+        }
+        __syncwarp();
       }
-      __syncwarp();
-      ++issued;
     }
     // Drain: every issued copy has landed before shared memory is released.
-    for (int i = issued > C::STAGES ? issued - C::STAGES : 0; i < issued; ++i)
+    for (int i = it > C::STAGES ? it - C::STAGES : 0; i < it; ++i)
       dev::mbar_wait(full0 + 8 * (i % C::STAGES), (i / C::STAGES) & 1, err, 100000000ull);
   } else if (warp == 1) {
     // Converged warp; the elected lane (lane 0) issues every MMA and commit.
     constexpr uint32_t idesc = dev::make_idesc_f16(C::BM, BN);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % C::STAGES;
-      const uint32_t ph = (kt / C::STAGES) & 1;
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(full0 + 8 * s, ph, err))) break;
+    int it = 0, i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      // the epilogue has drained this accumulator (tile i - 2)
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(tempty + 8 * buf, ((i >> 1) & 1) ^ 1, err))) break;
       dev::tc_fence_after();
-      const uint32_t sa = sbase + s * C::STAGE_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < C::BK / 16; ++kk) {
-        if (dev::elect_one()) {
-          const uint64_t ad = dev::make_sw128_desc(sa + kk * 32);
-          const uint64_t bd = dev::make_sw128_desc(sa + C::A_BYTES + kk * 32);
-          dev::tc_mma_f16(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % C::STAGES;
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(full0 + 8 * s, (it / C::STAGES) & 1, err))) {
+          ok = false;
+          break;
         }
+        dev::tc_fence_after();
+        const uint32_t sa = sbase + s * C::STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          if (dev::elect_one()) {
+            const uint64_t ad = dev::make_sw128_desc(sa + kk * 32);
+            const uint64_t bd = dev::make_sw128_desc(sa + C::A_BYTES + kk * 32);
+            dev::tc_mma_f16(tmem + buf * BN, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
+          __syncwarp();
+        }
+        if (dev::elect_one()) dev::tc_commit(empty0 + 8 * s);
         __syncwarp();
       }
-      if (dev::elect_one()) dev::tc_commit(empty0 + 8 * s);
+      if (!ok) break;
+      if (dev::elect_one()) dev::tc_commit(tfull + 8 * buf);
       __syncwarp();
     }
-    if (dev::elect_one()) dev::tc_commit(accum);
+    if (dev::elect_one()) dev::tc_commit(fin);
     __syncwarp();
     // All MMAs of this CTA have retired before TMEM is released below.
-    dev::mbar_wait(accum, 0, err, 100000000ull);
+    dev::mbar_wait(fin, 0, err, 100000000ull);
   } else {
     const int quarter = warp & 3;
-    const int row = m0 + quarter * 32 + lane;
-    if (__all_sync(0xffffffffu, dev::mbar_wait(accum, 0, err))) {  // warp-uniform: tcgen05.ld is collective
+    int i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      const int m0 = (t / n_tiles) * C::BM, nt = t % n_tiles, n0 = nt * BN;
+      const int row = m0 + quarter * 32 + lane;
+      // warp-uniform: tcgen05.ld is collective
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(tfull + 8 * buf, (i >> 1) & 1, err))) break;
       dev::tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + buf * BN;
       if (e.mode == kSkinnySwiglu) {
         // out[row][g] = f16(silu(f16 gate) * f16 up) for the tile's BN/2 outputs
 #pragma unroll 1
@@ -144,7 +177,7 @@ __global__ void __launch_bounds__(192, 1)
           dev::tmem_ld_32x32b_x32(tbase + BN / 2 + c, u);
           dev::tc_wait_ld();
           if (row < M) {
-            uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + blockIdx.x * (BN / 2) + c);
+            uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + nt * (BN / 2) + c);
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               float o[8];
@@ -163,22 +196,22 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       } else {
-      // RoPE: position of this token row within its request (ops.ts:188)
-      int pos = 0;
-      if (e.mode == kSkinnyRope && row < M) {
-        const int* off = e.merged ? e.meta->tgt_off : e.meta->src_off;
-        int b = 0;
-        while (b + 1 < e.meta->batch && row >= off[b + 1]) ++b;
-        pos = row - off[b];
-      }
+        // RoPE: position of this token row within its request (ops.ts:188)
+        int pos = 0;
+        if (e.mode == kSkinnyRope && row < M) {
+          const int* off = e.merged ? e.meta->tgt_off : e.meta->src_off;
+          int b = 0;
+          while (b + 1 < e.meta->batch && row >= off[b + 1]) ++b;
+          pos = row - off[b];
+        }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = n0 + c * 32;
-        if (e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = n0 + c * 32;
           uint32_t r[32];
           dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
           dev::tc_wait_ld();
-          if (row < M) {
+          // no early exit: every lane reaches the next (warp-collective) tcgen05.ld
+          if (row < M && e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
             // (even, odd) column pairs rotated by the table row of pos, as the
             // f16-stored QKV would be (k_misc.cu rope_kernel)
             const float* cs = e.rope + ((size_t)pos * 64 + ((col0 & 127) >> 1)) * 2;
@@ -187,9 +220,9 @@ __global__ void __launch_bounds__(192, 1)
             for (int p = 0; p < 16; ++p) {
               const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
               const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
-              const float2 t = *reinterpret_cast<const float2*>(cs + 2 * p);
-              const float first = __fsub_rn(__fmul_rn(even, t.x), __fmul_rn(odd, t.y));
-              const float second = __fadd_rn(__fmul_rn(even, t.y), __fmul_rn(odd, t.x));
+              const float2 tc = *reinterpret_cast<const float2*>(cs + 2 * p);
+              const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
+              const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
               __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
               o[p] = *reinterpret_cast<uint32_t*>(&h);
             }
@@ -198,14 +231,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-          }
-          continue;
-        }
-        uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
-        dev::tc_wait_ld();
-        if (row < M) {
-          uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + n0 + c * 32);
+          } else if (row < M) {
+          uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + col0);
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             uint4 u;
@@ -215,9 +242,11 @@ __global__ void __launch_bounds__(192, 1)
               h[j] = __floats2half2_rn(__uint_as_float(r[v * 8 + 2 * j]), __uint_as_float(r[v * 8 + 2 * j + 1]));
             dst[v] = u;
           }
+          }
         }
       }
-      }
+      dev::tc_fence_before();
+      dev::mbar_arrive(tempty + 8 * buf);
     }
   }
   dev::tc_fence_before();
@@ -233,6 +262,7 @@ cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, i
                       int max_rows, int n, int k, uint32_t* err, const GemmEpi& ep, cudaStream_t s) {
   using C = GemmCfg<BN>;
   static bool configured[64] = {};
+  static int sms[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -240,10 +270,15 @@ cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, i
   if (!configured[dev]) {
     e = cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(n / BN, (max_rows + C::BM - 1) / C::BM);
-  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, err, ep);
+  // One CTA per SM (shared memory and TMEM allow one), never more than tiles.
+  const int n_tiles = n / BN;
+  const long long tiles = (long long)((max_rows + C::BM - 1) / C::BM) * n_tiles;
+  const int grid = (int)std::min<long long>(sms[dev], std::max<long long>(tiles, 1));
+  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, n_tiles, err, ep);
   return cudaGetLastError();
 }
 
