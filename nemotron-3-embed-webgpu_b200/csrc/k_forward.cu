@@ -75,6 +75,19 @@ __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* er
 
 __device__ __forceinline__ void pw_sync() { dev::named_barrier(1, 128); }
 
+// Release/acquire hand-offs between CTAs. A sequentially consistent fence
+// (__threadfence) costs 1.5-3 us here while the weight stream is in flight;
+// these need only release (publish this CTA's writes, ordered before by the
+// named barrier) and acquire (see the other CTAs' writes).
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -357,8 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     auto grid_barrier = [&]() {
       pw_sync();
       if (pt == 0) {
-        __threadfence();
-        atomicAdd(&a.sync[0], 1u);
+        red_add_release(&a.sync[0], 1u);
         const uint32_t target = (++nbar) * (uint32_t)G;
         if (!ld_err(err)) {
           const uint64_t t0 = dev::globaltimer();
@@ -373,8 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
             }
           }
         }
-        __threadfence();
-        // X tiles of the next phase are read by TMA (async proxy) after this.
+        // (the acquire loads above order what follows) X tiles of the next
+        // phase are read by TMA (async proxy) after this.
         dev::fence_proxy_async_global();
       }
       pw_sync();
@@ -462,11 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       if (pt == 0) {
         int last = 0;
         if (!ld_err(err)) {
-          __threadfence();
           const int idx = sg.proj * kFwdMaxTiles + sg.tile;
-          const uint32_t old = atomicAdd(&a.sync[1 + idx], 1u);
+          const uint32_t old = atom_add_acq_rel(&a.sync[1 + idx], 1u);
           last = old + 1 == (uint32_t)nslots[idx];
-          if (last) __threadfence();
         }
         sh->flag = last;
       }
