@@ -10,16 +10,20 @@
 // Scores and the softmax statistics are f32, P is rounded to f16 for the P.V
 // product (the reference keeps P in f16 as well), O accumulates in f32.
 //
-// One CTA = 128 queries of one q head of one request (192 threads):
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               (double-buffered ring); V comes straight out of the QKV
+// One CTA = two tiles of 128 queries (256) of one q head of one request, which
+// share every K/V tile (320 threads):
+//   warp 0      TMA producer: the two Q tiles once, then K and V tiles of 128
+//               keys (double-buffered ring); V comes straight out of the QKV
 //               projection buffer and is consumed MN-major
-//   warp 1      TMEM allocation (512 columns: S ping-pong 2 x 128, O 128) and
-//               tcgen05.mma issue (elected lane): S_j = Q.K_j^T, O += P_j.V_j
-//   warps 2..5  softmax (thread = query row): tcgen05.ld of the S row, online
-//               max/sum, P_j (f16) into 128B-swizzled shared memory, O row
-//               rescaled in TMEM (tcgen05.ld/st) when the running max moves;
-//               final O / l to global.
+//   warp 1      TMEM allocation (512 columns: S_0, S_1, O_0, O_1, 128 each) and
+//               tcgen05.mma issue (elected lane): S_t = Q_t.K_j^T, then
+//               O_t += P_t.V_j with P_t read from TMEM (A operand in tensor
+//               memory), interleaved over the two tiles so the tensor pipe
+//               works on one tile while the other tile's softmax runs
+//   warps 2..5  softmax of tile 0, warps 6..9 of tile 1 (thread = query row):
+//               tcgen05.ld of the S row, online max/sum, P (f16) written back
+//               over its own S columns, O row rescaled in TMEM when the running
+//               max moves; final O / l to global.
 // All mbarrier waits are bounded; on a timeout every role unwinds and TMEM is
 // released only after the CTA's MMAs have retired.
 #include "kernels.cuh"
@@ -30,20 +34,20 @@ namespace {
 constexpr int kTile = 128;
 constexpr int kHalfTile = kTile * 64 * 2;  // 128 rows x 64 f16 = 16 KB (one 128B-swizzle column block)
 constexpr int kTileBytes = 2 * kHalfTile;  // 128 x 128 f16
-constexpr int kSmem = 1024 + kTileBytes /*Q*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ + kTileBytes /*P*/ + 256;
+constexpr int kThreadsA = 320;
+constexpr int kSmem = 1024 + 2 * kTileBytes /*Q_0, Q_1*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ + 256;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;
-
-__device__ __forceinline__ void st_p_chunk(uint8_t* p_tile, int r, int c, uint4 v) {
-  // K-major 128B-swizzled: column block c/8 (64 keys), 16-byte chunk c%8.
-  uint8_t* blk = p_tile + (c >> 3) * kHalfTile;
-  const int cc = c & 7;
-  *reinterpret_cast<uint4*>(blk + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
-}
+constexpr uint32_t kColS = 0, kColO = 256;  // S_t at kColS + 128 t, O_t at kColO + 128 t
 
 __device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 struct AttnTcArgs {
@@ -55,18 +59,19 @@ struct AttnTcArgs {
   int out_ld;  // output row stride (q heads of the group x 128)
 };
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreadsA, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_kc,
                         const __grid_constant__ CUtensorMap map_vc, AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   dev::pdl_launch_dependents();
-  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kTile;
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * 2 * kTile;
   const Meta* meta = a.meta;
   if (b >= meta->batch) return;
   const int ph = a.merged ? 1 : 0;
   const int len = a.merged ? meta->tgt_len[b] : meta->src_len[b];
   if (q0 >= len) return;  // uniform over the CTA
+  const int nqt = q0 + kTile < len ? 2 : 1;  // query tiles with valid rows
   const int base = a.merged ? meta->tgt_off[b] : meta->src_off[b];
   const int kvh = h / (kQHeads / kKVHeads);
   const bool sampled = !meta->exact && len > kSampleThreshold;
@@ -80,16 +85,15 @@ __global__ void __launch_bounds__(192, 1)
 
   const uint32_t raw_s = dev::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sQ = smem;                    // Q_0, Q_1
+  uint8_t* sK = sQ + 2 * kTileBytes;
   uint8_t* sV = sK + 2 * kTileBytes;
-  uint8_t* sP = sV + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
   const uint32_t q_full = dev::smem_u32(bars);
   const uint32_t kv_full = q_full + 8, kv_empty = kv_full + 16;
-  const uint32_t s_full = kv_empty + 16, p_ready = s_full + 16, pv_done = p_ready + 8;
-  const uint32_t mma_fin = pv_done + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  const uint32_t s_full = kv_empty + 16, p_ready = s_full + 16, pv_done = p_ready + 16;
+  const uint32_t mma_fin = pv_done + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == 0 && lane == 0) {
@@ -101,9 +105,9 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_init(kv_full + 8 * s, 1);
       dev::mbar_init(kv_empty + 8 * s, 1);
       dev::mbar_init(s_full + 8 * s, 1);
+      dev::mbar_init(p_ready + 8 * s, 128);
+      dev::mbar_init(pv_done + 8 * s, 1);
     }
-    dev::mbar_init(p_ready, 128);
-    dev::mbar_init(pv_done, 1);
     dev::mbar_init(mma_fin, 1);
     dev::fence_mbar_init();
   }
@@ -120,9 +124,12 @@ __global__ void __launch_bounds__(192, 1)
     // Converged warp; the elected lane issues the copies.
     dev::pdl_wait();
     if (dev::elect_one()) {
-      dev::mbar_arrive_expect_tx(q_full, kTileBytes);
-      dev::tma_load_2d(dev::smem_u32(sQ), &map_q, h * kHeadDim, base + q0, q_full);
-      dev::tma_load_2d(dev::smem_u32(sQ + kHalfTile), &map_q, h * kHeadDim + 64, base + q0, q_full);
+      dev::mbar_arrive_expect_tx(q_full, nqt * kTileBytes);
+      for (int t = 0; t < nqt; ++t) {
+        dev::tma_load_2d(dev::smem_u32(sQ + t * kTileBytes), &map_q, h * kHeadDim, base + q0 + t * kTile, q_full);
+        dev::tma_load_2d(dev::smem_u32(sQ + t * kTileBytes + kHalfTile), &map_q, h * kHeadDim + 64,
+                         base + q0 + t * kTile, q_full);
+      }
     }
     __syncwarp();
     int issued = 0;
@@ -147,69 +154,78 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_wait(kv_full + 8 * (i & 1), (i >> 1) & 1, a.err, 100000000ull);
   } else if (warp == 1) {
     // Converged warp; the elected lane (lane 0) issues every MMA and commit.
-    const uint32_t idesc_s = dev::make_idesc_f16(kTile, kTile);             // Q.K^T, both K-major
+    // Order per key tile j and query tile t: PV_t(j-1) (reads P_t from the
+    // S_t columns) strictly before S_t(j) (overwrites them); the tensor pipe
+    // runs them in issue order.
+    const uint32_t idesc_s = dev::make_idesc_f16(kTile, kTile);                  // Q.K^T, both K-major
     const uint32_t idesc_o = dev::make_idesc_f16(kTile, kHeadDim) | (1u << 16);  // P.V, V MN-major
-    const uint32_t aq = dev::smem_u32(sQ), ap = dev::smem_u32(sP);
     bool ok = __all_sync(0xffffffffu, dev::mbar_wait(q_full, 0, a.err));
-    auto pv = [&](int i) -> bool {
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(p_ready, i & 1, a.err))) return false;
+    auto pv = [&](int t, int jj) -> bool {  // O_t += P_t(jj) . V(jj)
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(p_ready + 8 * t, jj & 1, a.err))) return false;
       dev::tc_fence_after();
-      const uint32_t bv = dev::smem_u32(sV + (i & 1) * kTileBytes);
+      const uint32_t bv = dev::smem_u32(sV + (jj & 1) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
         if (dev::elect_one()) {
-          const uint64_t ad = dev::make_sw128_desc(ap + (kk >> 2) * kHalfTile + (kk & 3) * 32);
           const uint64_t bd = dev::make_sw128_desc_mn(bv + kk * 2048, kHalfTile, 1024);
-          dev::tc_mma_f16(tmem + kColO, ad, bd, idesc_o, (i | kk) != 0 ? 1u : 0u);
+          dev::tc_mma_f16_ts(tmem + kColO + t * kTile, tmem + kColS + t * kTile + kk * 8, bd, idesc_o,
+                             (jj | kk) != 0 ? 1u : 0u);
         }
         __syncwarp();
       }
-      if (dev::elect_one()) {
-        dev::tc_commit(pv_done);
-        dev::tc_commit(kv_empty + 8 * (i & 1));
-      }
+      if (dev::elect_one()) dev::tc_commit(pv_done + 8 * t);
       __syncwarp();
       return true;
     };
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j & 1;
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full + 8 * st, (j >> 1) & 1, a.err))) {
-        ok = false;
-        break;
-      }
-      dev::tc_fence_after();
-      const uint32_t bk = dev::smem_u32(sK + st * kTileBytes);
+    auto qk = [&](int t, int j) {  // S_t = Q_t . K(j)^T
+      const uint32_t aq = dev::smem_u32(sQ + t * kTileBytes);
+      const uint32_t bk = dev::smem_u32(sK + (j & 1) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kHeadDim / 16; ++kk) {
         if (dev::elect_one()) {
           const uint64_t ad = dev::make_sw128_desc(aq + (kk >> 2) * kHalfTile + (kk & 3) * 32);
           const uint64_t bd = dev::make_sw128_desc(bk + (kk >> 2) * kHalfTile + (kk & 3) * 32);
-          dev::tc_mma_f16(tmem + kColS + st * kTile, ad, bd, idesc_s, kk != 0 ? 1u : 0u);
+          dev::tc_mma_f16(tmem + kColS + t * kTile, ad, bd, idesc_s, kk != 0 ? 1u : 0u);
         }
         __syncwarp();
       }
-      if (dev::elect_one()) dev::tc_commit(s_full + 8 * st);
+      if (dev::elect_one()) dev::tc_commit(s_full + 8 * t);
       __syncwarp();
-      if (j >= 1) ok = pv(j - 1);
+    };
+    for (int j = 0; j < ntiles && ok; ++j) {
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full + 8 * (j & 1), (j >> 1) & 1, a.err))) {
+        ok = false;
+        break;
+      }
+      dev::tc_fence_after();
+      for (int t = 0; t < nqt && ok; ++t) {
+        if (j > 0) ok = pv(t, j - 1);
+        if (ok) qk(t, j);
+      }
+      // every MMA that reads key/value stage j - 1 has been issued
+      if (ok && j > 0 && dev::elect_one()) dev::tc_commit(kv_empty + 8 * ((j - 1) & 1));
+      __syncwarp();
     }
-    if (ok) pv(ntiles - 1);
+    for (int t = 0; t < nqt && ok; ++t) ok = pv(t, ntiles - 1);
     if (dev::elect_one()) dev::tc_commit(mma_fin);
     __syncwarp();
     dev::mbar_wait(mma_fin, 0, a.err, 100000000ull);  // every MMA retired before TMEM is freed
   } else {
-    // ---- softmax warps: thread = query row (TMEM lane) ----
+    // ---- softmax warps: tile t, thread = query row (TMEM lane) ----
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int pos = q0 + row;
+    const uint32_t colS = kColS + t * kTile, colO = kColO + t * kTile;
+    const int pos = q0 + t * kTile + row;
     const float temp = pos >= 16384 ? logf(floorf((float)pos / 16384.0f) + 1.0f) * 0.1f + 1.0f : 1.0f;
-    const float scale = 0.08838834764831845f * temp;
+    // exp(x) = 2^(x log2 e): scores are kept in log2 units
+    const float scale = 0.08838834764831845f * temp * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
-    bool ok = true;
+    bool ok = t < nqt;  // uniform over the warp
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j & 1;
       // warp-uniform outcome: the TMEM loads below are warp-collective
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(s_full + 8 * st, (j >> 1) & 1, a.err))) {
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(s_full + 8 * t, j & 1, a.err))) {
         ok = false;
         break;
       }
@@ -218,7 +234,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(lane_base + kColS + st * kTile + c * 32, r);
+        dev::tmem_ld_32x32b_x32(lane_base + colS + c * 32, r);
         dev::tc_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
@@ -234,13 +250,22 @@ __global__ void __launch_bounds__(192, 1)
       float rsum = 0.f;
 #pragma unroll
       for (int i = 0; i < kTile; ++i) {
-        s[i] = __expf(s[i] - mnew);
+        s[i] = ex2(s[i] - mnew);
         rsum += s[i];
       }
-      const float alpha = __expf(m - mnew);  // 0 on the first tile
+      const float alpha = ex2(m - mnew);  // 0 on the first tile
+      // P_t (f16) over its own S columns: S_t(j) has been read, and neither
+      // PV_t(j) nor S_t(j + 1) is issued before p_ready
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pr[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pr[i] = pack_h2f(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
+        dev::tmem_st_32x32b_x32(lane_base + colS + c * 32, pr);
+      }
       if (j > 0) {
-        // PV_{j-1} complete: O is stable and the P buffer is free.
-        if (!__all_sync(0xffffffffu, dev::mbar_wait(pv_done, (j - 1) & 1, a.err))) {
+        // PV_t(j - 1) complete: O_t is stable
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(pv_done + 8 * t, (j - 1) & 1, a.err))) {
           ok = false;
           break;
         }
@@ -249,34 +274,28 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
-            dev::tmem_ld_32x32b_x32(lane_base + kColO + c * 32, r);
+            dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
             dev::tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            dev::tmem_st_32x32b_x32(lane_base + kColO + c * 32, r);
+            dev::tmem_st_32x32b_x32(lane_base + colO + c * 32, r);
           }
-          dev::tc_wait_st();
         }
       }
+      dev::tc_wait_st();
       l = l * alpha + rsum;
       m = mnew;
-#pragma unroll
-      for (int c = 0; c < kTile / 8; ++c)
-        st_p_chunk(sP, row, c,
-                   make_uint4(pack_h2f(s[c * 8], s[c * 8 + 1]), pack_h2f(s[c * 8 + 2], s[c * 8 + 3]),
-                              pack_h2f(s[c * 8 + 4], s[c * 8 + 5]), pack_h2f(s[c * 8 + 6], s[c * 8 + 7])));
-      dev::fence_proxy_async_smem();
       dev::tc_fence_before();
-      dev::mbar_arrive(p_ready);
+      dev::mbar_arrive(p_ready + 8 * t);
     }
-    if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done, (ntiles - 1) & 1, a.err))) {
+    if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done + 8 * t, (ntiles - 1) & 1, a.err))) {
       dev::tc_fence_after();
       const float inv = 1.0f / l;
       __half* dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(lane_base + kColO + c * 32, r);
+        dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
         dev::tc_wait_ld();
         if (pos < len) {
 #pragma unroll
@@ -360,8 +379,8 @@ cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bo
     configured[dev] = true;
   }
   AttnTcArgs a{meta, merged ? 1 : 0, out, err, v_col0, out_ld};
-  dim3 grid((max_len + kTile - 1) / kTile, q_heads, batch);
-  attention_tc_kernel<<<grid, 192, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
+  dim3 grid((max_len + 2 * kTile - 1) / (2 * kTile), q_heads, batch);
+  attention_tc_kernel<<<grid, kThreadsA, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
   return cudaGetLastError();
 }
 
