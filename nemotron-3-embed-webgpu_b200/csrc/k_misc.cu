@@ -346,7 +346,22 @@ __global__ void __launch_bounds__(256) pool_kernel(const __half* __restrict__ nr
   const size_t base = (size_t)meta->tgt_off[b];
   const int c = threadIdx.x * 8;
   float t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int p = 0; p < len; ++p) {
+  // rows summed in order; 16 row loads in flight per thread
+  constexpr int kRows = 16;
+  int p = 0;
+  for (; p + kRows <= len; p += kRows) {
+    uint4 u[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) u[r] = *reinterpret_cast<const uint4*>(nrm + (base + p + r) * kHidden + c);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      float a[8];
+      unpack8(u[r], a);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = __fadd_rn(t[i], a[i]);
+    }
+  }
+  for (; p < len; ++p) {
     float a[8];
     unpack8(*reinterpret_cast<const uint4*>(nrm + (base + p) * kHidden + c), a);
 #pragma unroll
