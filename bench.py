@@ -64,14 +64,16 @@ def workload_lengths(name: str, seed: int) -> list:
     return list(spec)
 
 
-def kernels_per_forward(n_layers: int, fused: bool, max_tokens: int) -> int:
+def kernels_per_forward(n_layers: int, fused: bool, seq: int) -> int:
     if fused:
         return 2  # run metadata + the persistent single-launch forward
-    # meta, embedding, first RMSNorm; per layer QKV, RoPE, attention, O, norm,
-    # gate/up, SwiGLU, down, norm (RoPE and SwiGLU live in the projection
-    # epilogues of the small-token kernels); merge; pool.
-    per_layer = 7 if max_tokens <= 64 else 9
-    return 3 + per_layer * n_layers + 2
+    # meta, embedding, first RMSNorm; per layer QKV, attention, O, norm,
+    # gate/up, down, norm (RoPE and SwiGLU live in the projection epilogues),
+    # plus the compact-key gather in layers whose valid length can exceed 2048;
+    # merge; pool.
+    merged_seq = synth_merged(seq)
+    gathers = (4 if seq > 2048 else 0) + ((n_layers - 4) if merged_seq > 2048 else 0)
+    return 3 + 7 * n_layers + gathers + 2
 
 
 # DRAM bytes (read + write) per launch of the single-launch forward, from one
@@ -392,7 +394,7 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "req/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "clocks": clocks.summary(),
-            "gpu_launches": kernels_per_forward(info.n_layers, fused, batch * seq) * args.steps}
+            "gpu_launches": kernels_per_forward(info.n_layers, fused, seq) * args.steps}
     print(json.dumps(line), flush=True)
 
 
