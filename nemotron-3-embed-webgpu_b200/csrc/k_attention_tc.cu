@@ -230,15 +230,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         break;
       }
       dev::tc_fence_after();
+      // the row's four 32-column loads are all in flight before one wait
+      uint32_t sr[kTile];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        dev::tmem_ld_32x32b_x32(lane_base + colS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      dev::tc_wait_ld();
       float s[kTile];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(lane_base + colS + c * 32, r);
-        dev::tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-      }
+      for (int i = 0; i < kTile; ++i) s[i] = __uint_as_float(sr[i]);
       const int valid = min(kTile, nkeys - j * kTile);
       float tmax = -INFINITY;
 #pragma unroll
@@ -271,15 +271,16 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         }
         dev::tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+          uint32_t orow[kHeadDim];  // all four loads in flight before one wait
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
-            dev::tc_wait_ld();
+          for (int c = 0; c < 4; ++c)
+            dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&orow[c * 32]));
+          dev::tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            dev::tmem_st_32x32b_x32(lane_base + colO + c * 32, r);
-          }
+          for (int i = 0; i < kHeadDim; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            dev::tmem_st_32x32b_x32(lane_base + colO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&orow[c * 32]));
         }
       }
       dev::tc_wait_st();
