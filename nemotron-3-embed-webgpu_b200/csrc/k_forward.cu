@@ -14,7 +14,7 @@
 // for activations.
 //
 //   warp 0      producer: cp.async.bulk of packed 128 x 256 weight chunks
-//               into a 3-stage ring, for all segments back to back
+//               into a 4-stage ring, for all segments back to back
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
 //               D[128 rows x NP tokens] (+)= A[128 x 64] . X^T[64 x NP] per
 //               substage, D double-buffered in TMEM across segments
@@ -46,7 +46,7 @@ using namespace tsd;
 
 constexpr int kThreads = 448;
 constexpr int kPhaseThread0 = 320;  // warps 10..13
-constexpr int kRawStages = 3;
+constexpr int kRawStages = 4;   // packed weight chunks in shared memory
 constexpr int kASlabs = 3;     // decoded A slabs in TMEM (128 x 256 f16 = 128 columns each)
 constexpr int kXStages = 4;
 constexpr uint32_t kTmemCols = 512;
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   // shared layout: X ring | epilogue slots | raw weight ring | barriers
   uint8_t* xring = smem;
   float* ebuf = reinterpret_cast<float*>(xring + kXStages * kXBytes);
-  uint8_t* raw = reinterpret_cast<uint8_t*>(ebuf) + (size_t)a.max_slots * kSlotBytes;
+  uint8_t* raw = reinterpret_cast<uint8_t*>(ebuf) + (size_t)a.scratch_slots * kSlotBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + ((kRawStages * CM + 15) & ~15));
   const uint32_t rfull = dev::smem_u32(bars), rempty = rfull + 8 * kRawStages;
   const uint32_t afull = rempty + 8 * kRawStages, aempty = afull + 8 * kASlabs;
@@ -893,16 +893,25 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
 
 }  // namespace
 
-size_t forward_smem_bytes(int chunk_max, int max_slots, int max_segs, int n_layers) {
+int forward_scratch_slots(int gate_up_slots, int residual_slots) {
+  constexpr int kSlot = kFwdNP * 128 * 4, kXRing = kXStages * 4 * kFwdNP * 128;
+  // norm_row stages [16 tiles][slots][128] f32 of the residual projection and
+  // the f16 residual row from the start of the X ring onwards.
+  const int stage = (kHidden / 128) * residual_slots * 128 * 4 + kHidden * 2;
+  const int over = stage > kXRing ? (stage - kXRing + kSlot - 1) / kSlot : 0;
+  return gate_up_slots > over ? gate_up_slots : over;
+}
+
+size_t forward_smem_bytes(int chunk_max, int scratch_slots, int max_segs, int n_layers) {
   constexpr int kXBytes = 4 * kFwdNP * 128;
-  return 1024 + (size_t)kXStages * kXBytes + (size_t)max_slots * kFwdNP * 128 * 4 +
+  return 1024 + (size_t)kXStages * kXBytes + (size_t)scratch_slots * kFwdNP * 128 * 4 +
          (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6) +
          ((sizeof(Shared) + 15) & ~15) + (size_t)max_segs * sizeof(FwdSeg) + sizeof(Meta) + 16 + kFwdNP * 128 * 4 +
          (size_t)n_layers * 4 * (4 + kFwdMaxTiles);
 }
 
 cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
-  if (grid < 1 || a.max_slots < 1) return cudaErrorInvalidValue;
+  if (grid < 1 || a.max_slots < 1 || a.scratch_slots < 1) return cudaErrorInvalidValue;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -916,7 +925,7 @@ cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = forward_smem_bytes(a.chunk_max, a.max_slots, a.max_segs, a.n_layers);
+  cfg.dynamicSmemBytes = forward_smem_bytes(a.chunk_max, a.scratch_slots, a.max_segs, a.n_layers);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barriers rely on it

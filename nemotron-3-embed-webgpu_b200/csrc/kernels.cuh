@@ -209,7 +209,9 @@ struct FwdArgs {
   int rope_rows;            // positions in the RoPE table (the plan's sequence, <= kFwdNP here)
   __half *x, *nrm, *xm, *nm, *qkv, *q, *k, *attn, *delta, *ffn;
   float* part;              // [tile][kFwdNP tokens][sstride slots][128] f32 per projection
-  int max_slots;
+  int max_slots;             // most split-K slots of any tile (sizes `part`)
+  int scratch_slots;         // 8 KB units of shared scratch after the X ring: the gate/up
+                             // epilogue's slots and the norm phase's O/down staging
   int max_segs;             // most segments any CTA owns
   float* out;               // [batch x 2048]
   int n_layers;
@@ -217,7 +219,10 @@ struct FwdArgs {
   int exact;                // no merge, pool over the unmerged rows
 };
 
-size_t forward_smem_bytes(int chunk_max, int max_slots, int max_segs, int n_layers);
+size_t forward_smem_bytes(int chunk_max, int scratch_slots, int max_segs, int n_layers);
+// Shared scratch (8 KB units) that the forward needs beyond its X ring, given
+// the most slots of a gate/up tile and of an O or down tile.
+int forward_scratch_slots(int gate_up_slots, int residual_slots);
 
 // Largest co-resident grid (one CTA per SM) or 0 if the kernel does not fit.
 cudaError_t forward_max_grid(size_t smem_bytes, int* grid);

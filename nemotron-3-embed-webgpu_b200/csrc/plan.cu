@@ -161,15 +161,22 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
     max_segs = std::max(max_segs, (int)per[c].size());
   }
   start[G] = (int)segs.size();
-  // The epilogue pulls all slots of a tile into shared memory at once.
-  const size_t smem = forward_smem_bytes(chunk_max, max_slots, max_segs, L);
+  std::vector<int> sstride((size_t)L * 4, 1);
+  for (int pi = 0; pi < L * 4; ++pi)
+    for (int t = 0; t < kFwdMaxTiles; ++t) sstride[pi] = std::max(sstride[pi], (int)nslots[(size_t)pi * kFwdMaxTiles + t]);
+  // The gate/up epilogue pulls all slots of a tile into shared memory at once,
+  // and the norms stage all O or down slots of a row.
+  int gu_slots = 1, res_slots = 1;
+  for (int l = 0; l < L; ++l) {
+    gu_slots = std::max(gu_slots, sstride[(size_t)l * 4 + 2]);
+    res_slots = std::max({res_slots, sstride[(size_t)l * 4 + 1], sstride[(size_t)l * 4 + 3]});
+  }
+  const int scratch_slots = forward_scratch_slots(gu_slots, res_slots);
+  const size_t smem = forward_smem_bytes(chunk_max, scratch_slots, max_segs, L);
   if (smem > 227 * 1024) return kOk;
   int resident = 0;
   NEMO_CUDA_TRY(forward_max_grid(smem, &resident));
   if (resident != G) return kOk;
-  std::vector<int> sstride((size_t)L * 4, 1);
-  for (int pi = 0; pi < L * 4; ++pi)
-    for (int t = 0; t < kFwdMaxTiles; ++t) sstride[pi] = std::max(sstride[pi], (int)nslots[(size_t)pi * kFwdMaxTiles + t]);
 
   FwdArgs& a = p.fargs;
   a = FwdArgs();
@@ -211,6 +218,7 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   a.delta = p.delta;
   a.ffn = p.ffn;
   a.max_slots = max_slots;
+  a.scratch_slots = scratch_slots;
   a.max_segs = max_segs;
   a.rope_rows = p.seq;
   a.out = p.out;
