@@ -204,23 +204,38 @@ __global__ void __launch_bounds__(192, 1)
           while (b + 1 < e.meta->batch && row >= off[b + 1]) ++b;
           pos = row - off[b];
         }
+        // The 32 table floats (16 cos/sin pairs, 128 contiguous bytes) of a
+        // chunk's rotated columns are loaded one chunk ahead, so their latency
+        // overlaps the previous chunk instead of following the TMEM load.
+        const bool rot_tile = e.mode == kSkinnyRope && row < M;
+        auto load_cs = [&](int c, float4 (&cs)[8]) {
+          const int col0 = n0 + c * 32;
+          if (rot_tile && c < BN / 32 && col0 < kQWidth + kKVWidth) {
+            const float4* src = reinterpret_cast<const float4*>(e.rope + ((size_t)pos * 64 + ((col0 & 127) >> 1)) * 2);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) cs[v] = __ldg(src + v);
+          }
+        };
+        float4 cs_cur[8], cs_nxt[8];
+        load_cs(0, cs_cur);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           const int col0 = n0 + c * 32;
           uint32_t r[32];
           dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
+          load_cs(c + 1, cs_nxt);
           dev::tc_wait_ld();
           // no early exit: every lane reaches the next (warp-collective) tcgen05.ld
           if (row < M && e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
             // (even, odd) column pairs rotated by the table row of pos, as the
             // f16-stored QKV would be (k_misc.cu rope_kernel)
-            const float* cs = e.rope + ((size_t)pos * 64 + ((col0 & 127) >> 1)) * 2;
+            const float* tcs = reinterpret_cast<const float*>(cs_cur);
             uint32_t o[16];
 #pragma unroll
             for (int p = 0; p < 16; ++p) {
               const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
               const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
-              const float2 tc = *reinterpret_cast<const float2*>(cs + 2 * p);
+              const float2 tc = make_float2(tcs[2 * p], tcs[2 * p + 1]);
               const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
               const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
               __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
@@ -243,6 +258,8 @@ __global__ void __launch_bounds__(192, 1)
             dst[v] = u;
           }
           }
+#pragma unroll
+          for (int v = 0; v < 8; ++v) cs_cur[v] = cs_nxt[v];
         }
       }
       dev::tc_fence_before();
