@@ -87,8 +87,9 @@ def measured_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 class NvmlClockSampler:
@@ -365,11 +366,17 @@ def run_ours(args) -> None:
         flops = 2.0 * 54_525_952 * (4 * tokens + (info.n_layers - 4) * merged)
         bound, unit, work = "tensor", "TFLOP/s", flops
         achieved = flops / (gemm_ms / 1e3) / 1e12
-        peak = peaks["bf16_tflops"]
+        # The projection GEMMs are timed inside back-to-back forwards of many
+        # milliseconds (a long step under the 1 kW cap), so the denominator is
+        # the sustained cuBLAS figure; the burst fraction is reported beside it.
+        peak = peaks["bf16_tflops_sustained"]
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
                 "traffic": NCU_TRAFFIC.get((args.workload, args.pack)) if fused else None, "kernel": kernel,
                 "kernel_ms_per_forward": gemm_ms, "algorithmic_per_forward": work,
-                "peak_source": peaks["source"], "stage_ms": prof}
+                "peak_source": peaks["source"] + (" (sustained bf16 GEMM)" if bound == "tensor" else " (copy)"),
+                "stage_ms": prof}
+    if bound == "tensor":
+        roofline["frac_of_burst_peak"] = achieved / peaks["bf16_tflops"]
 
     plan.destroy()
     model.destroy()
