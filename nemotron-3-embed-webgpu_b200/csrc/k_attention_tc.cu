@@ -22,8 +22,8 @@
 //               works on one tile while the other tile's softmax runs
 //   warps 2..5  softmax of tile 0, warps 6..9 of tile 1 (thread = query row):
 //               tcgen05.ld of the S row, online max/sum, P (f16) written back
-//               over its own S columns, O row rescaled in TMEM when the running
-//               max moves; final O / l to global.
+//               over its own S columns, O rows rescaled in TMEM when the running
+//               max moves (it moves only by more than 2^8); final O / l to global.
 // All mbarrier waits are bounded; on a timeout every role unwinds and TMEM is
 // released only after the CTA's MMAs have retired.
 #include "kernels.cuh"
@@ -38,6 +38,7 @@ constexpr int kThreadsA = 320;
 constexpr int kSmem = 1024 + 2 * kTileBytes /*Q_0, Q_1*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;  // S_t at kColS + 128 t, O_t at kColO + 128 t
+constexpr float kMaxSlack = 8.0f;           // running-max hysteresis (log2 units): P <= 256
 
 __device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
@@ -246,14 +247,20 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         s[i] = i < valid ? s[i] * scale : -INFINITY;
         tmax = fmaxf(tmax, s[i]);
       }
-      const float mnew = fmaxf(m, tmax);
+      // The running max of the warp's rows moves only when some row's tile
+      // max exceeds it by more than kMaxSlack (log2 units). Otherwise P is
+      // taken against the stale max: P <= 2^kMaxSlack, well inside f16, and
+      // O / l is unchanged, while the O rows need no rescale on that tile.
+      // (With the exact running max nearly every tile moves some row's max.)
+      const bool move = __any_sync(0xffffffffu, tmax > m + kMaxSlack);  // always on the first tile
+      const float mnew = move ? fmaxf(m, tmax) : m;
       float rsum = 0.f;
 #pragma unroll
       for (int i = 0; i < kTile; ++i) {
         s[i] = ex2(s[i] - mnew);
         rsum += s[i];
       }
-      const float alpha = ex2(m - mnew);  // 0 on the first tile
+      const float alpha = ex2(m - mnew);  // 0 on the first tile, 1 while the max stays
       // P_t (f16) over its own S columns: S_t(j) has been read, and neither
       // PV_t(j) nor S_t(j + 1) is issued before p_ready
 #pragma unroll
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           break;
         }
         dev::tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (move) {
           uint32_t orow[kHeadDim];  // all four loads in flight before one wait
 #pragma unroll
           for (int c = 0; c < 4; ++c)
