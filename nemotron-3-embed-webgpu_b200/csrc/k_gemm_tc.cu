@@ -50,7 +50,13 @@ __global__ void __launch_bounds__(192, 1)
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const int M = *d_rows;
-  const int total = (M + C::BM - 1) / C::BM * n_tiles;
+  const int KT = k / C::BK;
+  // Work units: (K split, m tile, n tile), n fastest; one split unless
+  // e.part asks for K-split partial sums (plain mode).
+  const int tiles = (M + C::BM - 1) / C::BM * n_tiles;
+  const int splits = e.part ? gemm_ksplit((M + C::BM - 1) / C::BM, n_tiles, KT, (int)gridDim.x) : 1;
+  const int total = tiles * splits;
+  if (e.splits_out && blockIdx.x == 0 && threadIdx.x == 0) *e.splits_out = splits;
   // 1024-byte alignment of the shared-window address (the 128-byte swizzle
   // pattern repeats every 1024 bytes and the descriptors assume base offset 0).
   const uint32_t raw_s = dev::smem_u32(smem_raw);
@@ -62,7 +68,6 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5);
   const uint32_t sbase = dev::smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = k / C::BK;
 
   if (warp == 0 && lane == 0) {
     dev::prefetch_tmap(&map_a);
@@ -93,8 +98,10 @@ __global__ void __launch_bounds__(192, 1)
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int m0 = (t / n_tiles) * C::BM, nt = t % n_tiles, n0 = nt * BN;
-      for (int kt = 0; kt < KT; ++kt, ++it) {
+      const int sp = t / tiles, tt = t % tiles;
+      const int m0 = (tt / n_tiles) * C::BM, nt = tt % n_tiles, n0 = nt * BN;
+      const int kt1 = (sp + 1) * KT / splits;
+      for (int kt = sp * KT / splits; kt < kt1; ++kt, ++it) {
         const int s = it % C::STAGES;
         if (!__all_sync(0xffffffffu, dev::mbar_wait(empty0 + 8 * s, ((it / C::STAGES) & 1) ^ 1, err))) {
           ok = false;
@@ -126,10 +133,11 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
       const int buf = i & 1;
+      const int sp = t / tiles, kt0 = sp * KT / splits, kt1 = (sp + 1) * KT / splits;
       // the epilogue has drained this accumulator (tile i - 2)
       if (!__all_sync(0xffffffffu, dev::mbar_wait(tempty + 8 * buf, ((i >> 1) & 1) ^ 1, err))) break;
       dev::tc_fence_after();
-      for (int kt = 0; kt < KT; ++kt, ++it) {
+      for (int kt = kt0; kt < kt1; ++kt, ++it) {
         const int s = it % C::STAGES;
         if (!__all_sync(0xffffffffu, dev::mbar_wait(full0 + 8 * s, (it / C::STAGES) & 1, err))) {
           ok = false;
@@ -142,7 +150,7 @@ __global__ void __launch_bounds__(192, 1)
           if (dev::elect_one()) {
             const uint64_t ad = dev::make_sw128_desc(sa + kk * 32);
             const uint64_t bd = dev::make_sw128_desc(sa + C::A_BYTES + kk * 32);
-            dev::tc_mma_f16(tmem + buf * BN, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+            dev::tc_mma_f16(tmem + buf * BN, ad, bd, idesc, (kt != kt0 || kk != 0) ? 1u : 0u);
           }
           __syncwarp();
         }
@@ -162,7 +170,8 @@ __global__ void __launch_bounds__(192, 1)
     int i = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
       const int buf = i & 1;
-      const int m0 = (t / n_tiles) * C::BM, nt = t % n_tiles, n0 = nt * BN;
+      const int sp = t / tiles, tt = t % tiles;
+      const int m0 = (tt / n_tiles) * C::BM, nt = tt % n_tiles, n0 = nt * BN;
       const int row = m0 + quarter * 32 + lane;
       // warp-uniform: tcgen05.ld is collective
       if (!__all_sync(0xffffffffu, dev::mbar_wait(tfull + 8 * buf, (i >> 1) & 1, err))) break;
@@ -246,6 +255,13 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+          } else if (row < M && splits > 1) {
+            // f32 partial sums of split sp (summed by the consumer in split order)
+            float4* dst = reinterpret_cast<float4*>(e.part + ((size_t)sp * M + row) * (n_tiles * BN) + col0);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
           } else if (row < M) {
           uint4* dst = reinterpret_cast<uint4*>(y + (size_t)row * ldy + col0);
 #pragma unroll
@@ -294,7 +310,8 @@ cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, i
   // One CTA per SM (shared memory and TMEM allow one), never more than tiles.
   const int n_tiles = n / BN;
   const long long tiles = (long long)((max_rows + C::BM - 1) / C::BM) * n_tiles;
-  const int grid = (int)std::min<long long>(sms[dev], std::max<long long>(tiles, 1));
+  // With K-split partial sums every SM takes units (gemm_ksplit sees the grid).
+  const int grid = ep.part ? sms[dev] : (int)std::min<long long>(sms[dev], std::max<long long>(tiles, 1));
   gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, n_tiles, err, ep);
   return cudaGetLastError();
 }
@@ -318,6 +335,8 @@ cudaError_t launch_gemm_tc_epi(const CUtensorMap* ma, const CUtensorMap* mb, __h
   if (k % 64 != 0 || n % bn != 0) return cudaErrorInvalidValue;
   if (ep.mode == kSkinnySwiglu && (bn < 128 || n != 2 * kInter)) return cudaErrorInvalidValue;
   if (ep.mode == kSkinnyRope && (n != kQKVWidth || !ep.meta || !ep.rope || !ep.q || !ep.k)) return cudaErrorInvalidValue;
+  if ((ep.part != nullptr) != (ep.splits_out != nullptr) || (ep.part && ep.mode != kSkinnyPlain))
+    return cudaErrorInvalidValue;
   switch (bn) {
     case 64: return launch_bn<64>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, ep, s);
     case 128: return launch_bn<128>(ma, mb, y, ldy, d_rows, max_rows, n, k, err, ep, s);

@@ -248,6 +248,67 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(__half* x, const __half* _
   *reinterpret_cast<uint4*>(norm + (size_t)row * kHidden + c) = pack8(o);
 }
 
+// rmsnorm_kernel after a GEMM launched with GemmEpi::part: when that GEMM
+// split K, the residual is f16(its f32 parts summed in split order), the f16
+// projection output an unsplit GEMM stores; otherwise its f16 output.
+__global__ void __launch_bounds__(256, 8) rmsnorm_parts_kernel(__half* x, const __half* __restrict__ residual,
+                                                            const float* __restrict__ part,
+                                                            const int* __restrict__ d_splits,
+                                                            const float* __restrict__ w, __half* norm,
+                                                            const int* __restrict__ d_rows, float eps) {
+  __shared__ float red[32];
+  dev::pdl_launch_dependents();
+  const int row = blockIdx.x;
+  const int M = *d_rows;
+  if (row >= M) return;
+  const int c = threadIdx.x * 8;
+  __half* xr = x + (size_t)row * kHidden + c;
+  // x, the f16 residual (always allocated; used with one split) and the
+  // split count are loaded together
+  const uint4 xv = *reinterpret_cast<const uint4*>(xr);
+  const uint4 rv = __ldcg(reinterpret_cast<const uint4*>(residual + (size_t)row * kHidden + c));
+  const int splits = *d_splits;
+  float r[8];
+  if (splits == 1) {
+    unpack8(rv, r);
+  } else {
+    {
+      const float4* p = reinterpret_cast<const float4*>(part + (size_t)row * kHidden + c);
+      const float4 a = __ldcg(p), b = __ldcg(p + 1);
+      r[0] = a.x, r[1] = a.y, r[2] = a.z, r[3] = a.w, r[4] = b.x, r[5] = b.y, r[6] = b.z, r[7] = b.w;
+    }
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4* p = reinterpret_cast<const float4*>(part + ((size_t)sp * M + row) * kHidden + c);
+      const float4 a = __ldcg(p), b = __ldcg(p + 1);
+      const float u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = __fadd_rn(r[i], u[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = __half2float(__float2half_rn(r[i]));
+  }
+  float v[8];
+  unpack8(xv, v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(v[i], r[i]);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  uint4 xs = pack8(v);  // x = f16(value)
+  *reinterpret_cast<uint4*>(xr) = xs;
+  ss = block_sum_256(ss, red);
+  const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)kHidden), eps));
+  float xn[8];
+  unpack8(xs, xn);
+  const float4 w0 = *reinterpret_cast<const float4*>(w + c);
+  const float4 w1 = *reinterpret_cast<const float4*>(w + c + 4);
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xn[i], inv), wv[i]);
+  *reinterpret_cast<uint4*>(norm + (size_t)row * kHidden + c) = pack8(o);
+}
+
 // ops.ts:168-194: one thread per (token, head, pair); the position is the
 // token's index within its (merged) row. A head group of nq q heads and nk kv
 // heads: Q at columns [0, nq*128) and K at [nq*128, (nq+nk)*128) of qkv rows
@@ -455,6 +516,14 @@ cudaError_t launch_embedding(const uint32_t* ids, const uint8_t* table, int voca
 cudaError_t launch_residual_rmsnorm(__half* x, const __half* residual, const float* w, __half* norm,
                                     const int* d_rows, int max_rows, cudaStream_t s) {
   rmsnorm_kernel<<<max_rows, 256, 0, s>>>(x, residual, w, norm, d_rows, kEpsilon);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_residual_rmsnorm_parts(__half* x, const __half* residual, const float* part, const int* d_splits,
+                                          const float* w, __half* norm, const int* d_rows, int max_rows,
+                                          cudaStream_t s) {
+  if (!residual || !part || !d_splits) return cudaErrorInvalidValue;
+  rmsnorm_parts_kernel<<<max_rows, 256, 0, s>>>(x, residual, part, d_splits, w, norm, d_rows, kEpsilon);
   return cudaGetLastError();
 }
 

@@ -49,6 +49,12 @@ cudaError_t launch_embedding(const uint32_t* ids, const uint8_t* table, int voca
 // ops.ts:21-72. rows = *d_rows (device int). residual may be null.
 cudaError_t launch_residual_rmsnorm(__half* x, const __half* residual, const float* w, __half* norm,
                                     const int* d_rows, int max_rows, cudaStream_t s);
+// The same after a persistent GEMM with GemmEpi::part: with one split
+// (*d_splits, the GEMM's GemmEpi::splits_out) the residual is its f16
+// output, else f16(sum of its f32 parts, in split order).
+cudaError_t launch_residual_rmsnorm_parts(__half* x, const __half* residual, const float* part, const int* d_splits,
+                                          const float* w, __half* norm, const int* d_rows, int max_rows,
+                                          cudaStream_t s);
 
 // ops.ts:168-194. merged selects the post-merge offsets for positions.
 cudaError_t launch_rope(const __half* qkv, const float* table, const Meta* meta, bool merged,
@@ -118,7 +124,37 @@ struct GemmEpi {
   const float* rope = nullptr;
   __half* q = nullptr;
   __half* k = nullptr;
+  // Plain mode only: with part set, the K range is split gemm_ksplit(...)
+  // ways and split s stores f32 partial sums at part[(s * M + row) * n + col]
+  // (M = valid rows); launch_residual_rmsnorm_parts sums them in split order.
+  // The split count used is stored at *splits_out (set with part).
+  float* part = nullptr;
+  int* splits_out = nullptr;
 };
+
+// K splits of the persistent GEMM for m_tiles x n_tiles output tiles of kt
+// 64-wide K steps on a grid of g CTAs. Few tiles, or a last wave that is
+// mostly empty, leave SMs idle (the O and down projections have 8 n tiles of
+// 256), so the K range may be split into up to 8 parts of >= 4 steps each.
+// The split with the smallest modelled time wins, in thousandths of one
+// full-K tile: waves of units, each 1/s of a tile plus 1/20 for its fill and
+// drain, plus the consumer's reads of the f32 partial sums (one 2048-wide f32
+// row per token and split, measured against a tile of kt steps at HBM speed).
+// Host and device evaluate the same integers.
+__host__ __device__ inline int gemm_ksplit(int m_tiles, int n_tiles, int kt, int g) {
+  const int tiles = m_tiles * n_tiles;
+  if (tiles <= 0 || g <= 0 || kt <= 0) return 1;
+  int best = 1, best_cost = 0x7fffffff;
+  for (int s = 1; s <= 8 && kt / s >= 4; ++s) {
+    const int waves = (tiles * s + g - 1) / g;
+    const int cost = waves * (1000 / s + 50) + (s > 1 ? s * m_tiles * 355 / kt : 0);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
 cudaError_t launch_gemm_tc_epi(const CUtensorMap* map_a, const CUtensorMap* map_b, __half* y, int ldy,
                                const int* d_rows, int max_rows, int n, int k, int bn, const GemmEpi& ep,
                                uint32_t* err, cudaStream_t s);

@@ -364,13 +364,22 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     if (np) {
       if (int rc = skinny(kProjO, &p.xmap_attn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
     } else if (p.batched_f16) {
-      NEMO_LAUNCH(launch_gemm_tc(&p.map_attn, &pr[kProjO].map[p.bn[l][1]], p.delta, kHidden, rows, maxr, kHidden,
-                                 kQWidth, kBnChoices[p.bn[l][1]], p.err, s));
+      GemmEpi ep;
+      ep.part = p.part;
+      ep.splits_out = p.part ? p.ksplit_used : nullptr;
+      NEMO_LAUNCH(launch_gemm_tc_epi(&p.map_attn, &pr[kProjO].map[2], p.delta, kHidden, rows, maxr, kHidden, kQWidth,
+                                     256, ep, p.err, s));
     } else if (int rc = gemm_q(kProjO, &p.map_attn, kSkinnyPlain, p.delta, kHidden)) {
       return rc;
     }
     stage(5);
-    NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, dm.ffn_norm[l], N, rows, maxr, s));
+    // the batched f16 O and down GEMMs may leave K-split partial sums
+    const bool parts = !np && p.batched_f16 && p.part;
+    if (parts)
+      NEMO_LAUNCH(
+          launch_residual_rmsnorm_parts(X, p.delta, p.part, p.ksplit_used, dm.ffn_norm[l], N, rows, maxr, s));
+    else
+      NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, dm.ffn_norm[l], N, rows, maxr, s));
     stage(6);
     if (np) {
       if (int rc = skinny(kProjGateUp, &p.xmap_norm[ph], kSkinnySwiglu, p.ffn, kInter)) return rc;
@@ -393,14 +402,20 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
     if (np) {
       if (int rc = skinny(kProjDown, &p.xmap_ffn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
     } else if (p.batched_f16) {
-      NEMO_LAUNCH(launch_gemm_tc(&p.map_ffn, &pr[kProjDown].map[p.bn[l][3]], p.delta, kHidden, rows, maxr, kHidden,
-                                 kInter, kBnChoices[p.bn[l][3]], p.err, s));
+      GemmEpi ep;
+      ep.part = p.part;
+      ep.splits_out = p.part ? p.ksplit_used + 1 : nullptr;
+      NEMO_LAUNCH(launch_gemm_tc_epi(&p.map_ffn, &pr[kProjDown].map[2], p.delta, kHidden, rows, maxr, kHidden, kInter,
+                                     256, ep, p.err, s));
     } else if (int rc = gemm_q(kProjDown, &p.map_ffn, kSkinnyPlain, p.delta, kHidden)) {
       return rc;
     }
     stage(9);
     const float* next = l + 1 < n_layers ? dm.attn_norm[l + 1] : dm.output_norm;
-    NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, next, N, rows, maxr, s));
+    if (parts)
+      NEMO_LAUNCH(launch_residual_rmsnorm_parts(X, p.delta, p.part, p.ksplit_used + 1, next, N, rows, maxr, s));
+    else
+      NEMO_LAUNCH(launch_residual_rmsnorm(X, p.delta, next, N, rows, maxr, s));
     if (dump) {
       const int T = merged ? host_meta.t1 : host_meta.t0;
       if (dump->tokens) dump->tokens[l] = T;
@@ -518,6 +533,19 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, b
   for (int l = 0; l < m->n_layers; ++l) {
     const int rows = l >= kMergeAfterLayer ? p.rows1 : p.rows0;
     for (int w = 0; w < 4; ++w) p.bn[l][w] = pick_bn(rows, kProjN[w]);
+  }
+  // Batched O and down (f16 weights): 2048 / 256 n tiles, K split on the
+  // device by gemm_ksplit for the valid token count; the partial-sum buffer
+  // covers every count up to the plan's rows.
+  NEMO_CUDA_TRY(cudaDeviceGetAttribute(&p.sms, cudaDevAttrMultiProcessorCount, p.device));
+  {
+    size_t need = 0;
+    for (int mt = 1; mt <= (int)(r0 / kGemmTileM); ++mt)
+      for (const int kt : {kQWidth / 64, kInter / 64}) {
+        const int sp = gemm_ksplit(mt, kHidden / 256, kt, p.sms);
+        if (sp > 1) need = std::max(need, (size_t)sp * mt * kGemmTileM * kHidden * 4);
+      }
+    if (need && (plan_alloc(p, &p.part, need) || plan_alloc(p, &p.ksplit_used, 2 * sizeof(int)))) return kErrCuda;
   }
   // Small-T path: worst-case tokens of the phase padded to the MMA N size.
   const int tmax[2] = {p.tmax0, p.tmax1};

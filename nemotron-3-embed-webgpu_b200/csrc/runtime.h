@@ -81,6 +81,12 @@ struct DevicePlan {
   __half *qkv = nullptr, *q = nullptr, *k = nullptr, *attn = nullptr, *delta = nullptr;
   __half *gu = nullptr, *ffn = nullptr;
   float* out = nullptr;
+  // K-split f32 partial sums of the batched O and down GEMMs (gemm_ksplit),
+  // sized for the largest split x rows any valid token count can use; sms is
+  // the grid of those GEMMs.
+  float* part = nullptr;
+  int* ksplit_used = nullptr;  // [2]: the K splits the last O and down GEMMs used
+  int sms = 0;
   // pinned host staging
   uint32_t* h_ids = nullptr;
   uint32_t* h_lengths = nullptr;
