@@ -133,17 +133,19 @@ struct GemmEpi {
 };
 
 // K splits of the persistent GEMM for m_tiles x n_tiles output tiles of kt
-// 64-wide K steps on a grid of g CTAs. Few tiles, or a last wave that is
-// mostly empty, leave SMs idle (the O and down projections have 8 n tiles of
-// 256), so the K range may be split into up to 8 parts of >= 4 steps each.
+// 64-wide K steps on a grid of g CTAs. Fewer tiles than CTAs leave SMs idle
+// for the whole launch (the O and down projections have 8 n tiles of 256),
+// so the K range may then be split into up to 8 parts of >= 4 steps each.
 // The split with the smallest modelled time wins, in thousandths of one
 // full-K tile: waves of units, each 1/s of a tile plus 1/20 for its fill and
 // drain, plus the consumer's reads of the f32 partial sums (one 2048-wide f32
-// row per token and split, measured against a tile of kt steps at HBM speed).
+// row per token and split, against a tile of kt steps). With a wave or more
+// of tiles no split is taken: at 200-320 tiles (one 3200-5000-token request)
+// splitting in two saved less in the GEMMs than the norms spent on partials.
 // Host and device evaluate the same integers.
 __host__ __device__ inline int gemm_ksplit(int m_tiles, int n_tiles, int kt, int g) {
   const int tiles = m_tiles * n_tiles;
-  if (tiles <= 0 || g <= 0 || kt <= 0) return 1;
+  if (tiles <= 0 || g <= 0 || kt <= 0 || tiles >= g) return 1;
   int best = 1, best_cost = 0x7fffffff;
   for (int s = 1; s <= 8 && kt / s >= 4; ++s) {
     const int waves = (tiles * s + g - 1) / g;
