@@ -72,11 +72,12 @@ int nemo_op_attention_tc(const void* d_q, const void* d_k, const void* d_qkv, co
  * attention runs (device memory owned by another allocator or reserved up
  * front; cudaFree would synchronise the whole device under a latency-bound
  * server). Its scratch is one fixed device array of 8 MiB + 256 B per GPU,
- * held until exit; calls needing more than 2048 sampled key rows (rows / 3 +
- * batch + 1 when max_len > 2048) fail with NEMO_ERR_ARGS. All calls share the
- * array: calls that overlap on the GPU race. The first call on a device looks
- * up the array's address; make it before any stream capture. Same arguments
- * and results as nemo_op_attention_tc. */
+ * held until exit. The call reads d_meta back to learn how many sampled key
+ * rows the run needs (requests longer than 2048 keep every third key; none in
+ * exact-attention metadata) and fails with NEMO_ERR_ARGS when that exceeds
+ * 2048. All calls share the array: calls that overlap on the GPU race. The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture. Same arguments and results as nemo_op_attention_tc. */
 int nemo_op_attention_tc_noalloc(const void* d_q, const void* d_k, const void* d_qkv, const void* d_meta, int merged,
                                  int batch, int max_len, int rows, void* d_out);
 
@@ -96,6 +97,28 @@ int nemo_op_pool(const void* d_norm, const void* d_meta, int batch, void* d_out)
  * M = *d_rows <= max_rows; d_x has max_rows rounded up to 128 rows. */
 int nemo_op_gemm(int impl, const void* d_x, const void* d_w, void* d_y, const void* d_rows,
                  int max_rows, int n, int k, int bn);
+
+/* Standalone quantised matmul, the operation of the reference's
+ * QuantMatmulKernel (src/webgpu/quant-matmul.ts:438-563: a GGUF Q4_K / Q6_K /
+ * Q4_0 or q4_0-tile32-compact weight buffer, an [m x k] f16 activation buffer,
+ * K divisible by 256, quant-matmul.ts:513), with f32 output:
+ *   Y[m x n] = X[m x k] . W[n x k]^T, W = f16(decode(blocks)).
+ * fmt is a NEMO_FMT_* value; n must be a multiple of 128.
+ *
+ * nemo_op_qmatmul_image_bytes / nemo_op_qmatmul_image re-tile the blocks on
+ * the device into the tile-slab image the projection kernels stream (what
+ * model load does for every projection); d_image is 256-byte aligned device
+ * memory of that size. nemo_op_qmatmul_enqueue runs the matmul on an image
+ * asynchronously on `stream` (a cudaStream_t, NULL = legacy default stream):
+ * the fused-dequant split-K kernel for m <= 64, the dequant-fused batched GEMM
+ * above. d_err is a zeroed 4-byte device word that becomes nonzero if a
+ * bounded wait gave up. nemo_op_qmatmul does all of it on packed blocks and
+ * synchronises (it allocates the image and error word and frees them). */
+size_t nemo_op_qmatmul_image_bytes(int fmt, int n, int k);
+int nemo_op_qmatmul_image(int fmt, const void* d_packed, int n, int k, void* d_image);
+int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m, int n, int k, void* d_y,
+                            void* d_err, void* stream);
+int nemo_op_qmatmul(int fmt, const void* d_packed, const void* d_x, int m, int n, int k, void* d_y);
 
 #ifdef __cplusplus
 }

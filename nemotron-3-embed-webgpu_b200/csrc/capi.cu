@@ -312,4 +312,60 @@ int nemo_op_gemm(int impl, const void* d_x, const void* d_w, void* d_y, const vo
   return kOk;
 }
 
+size_t nemo_op_qmatmul_image_bytes(int fmt, int n, int k) { return qmatmul_image_bytes(fmt, n, k); }
+
+int nemo_op_qmatmul_image(int fmt, const void* d_packed, int n, int k, void* d_image) {
+  if (!d_packed || !d_image || !qmatmul_image_bytes(fmt, n, k) || ((uintptr_t)d_image & 255) ||
+      ((uintptr_t)d_packed & 15)) {
+    set_error("nemo_op_qmatmul_image: bad arguments (n a multiple of 128, K divisible by 256, aligned buffers)");
+    return kErrArgs;
+  }
+  return sync_and_check(launch_qmatmul_retile(fmt, (const uint8_t*)d_packed, n, k, (uint8_t*)d_image, 0));
+}
+
+int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m, int n, int k, void* d_y, void* d_err,
+                            void* stream) {
+  if (!d_image || !d_x || !d_y || !d_err || m < 1 || ((uintptr_t)d_image & 255) || ((uintptr_t)d_x & 15) ||
+      ((uintptr_t)d_y & 15)) {
+    set_error("nemo_op_qmatmul_enqueue: bad arguments");
+    return kErrArgs;
+  }
+  return qmatmul_enqueue(fmt, (const uint8_t*)d_image, (const __half*)d_x, m, n, k, (float*)d_y, (uint32_t*)d_err,
+                         (cudaStream_t)stream);
+}
+
+int nemo_op_qmatmul(int fmt, const void* d_packed, const void* d_x, int m, int n, int k, void* d_y) {
+  if (!d_packed || !d_x || !d_y || m < 1) {
+    set_error("nemo_op_qmatmul: bad arguments");
+    return kErrArgs;
+  }
+  const size_t bytes = qmatmul_image_bytes(fmt, n, k);
+  if (!bytes) {
+    set_error("quantized matmul K must be divisible by 256 and n by 128");
+    return kErrArgs;
+  }
+  uint8_t* image = nullptr;
+  uint32_t* err = nullptr;
+  NEMO_CUDA_TRY(cudaMalloc(&image, bytes));
+  if (cudaMalloc(&err, 4) != cudaSuccess || cudaMemset(err, 0, 4) != cudaSuccess) {
+    cudaFree(image);
+    cudaFree(err);
+    set_error("nemo_op_qmatmul: device allocation failed");
+    return kErrCuda;
+  }
+  int rc = nemo_op_qmatmul_image(fmt, d_packed, n, k, image);
+  if (!rc) rc = nemo_op_qmatmul_enqueue(fmt, image, d_x, m, n, k, d_y, err, nullptr);
+  if (!rc) rc = sync_and_check(cudaGetLastError());
+  uint32_t h = 0;
+  if (!rc && cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) rc = kErrCuda;
+  cudaFree(image);
+  cudaFree(err);
+  if (rc) return rc;
+  if (h) {
+    set_error("quantized matmul: a bounded wait timed out");
+    return kErrTimeout;
+  }
+  return kOk;
+}
+
 }  // extern "C"

@@ -57,12 +57,12 @@ template <int MB>
 __global__ void __launch_bounds__(kQThreads, 1)
     gemm_q_kernel(const __grid_constant__ CUtensorMap map_x, const uint8_t* __restrict__ packed,
                   const SkinnyTile* __restrict__ tiles, int slabs, int chunk_max, int mode, __half* y, int ldy,
-                  const int* __restrict__ d_rows, uint32_t* err) {
+                  const int* __restrict__ d_rows, int rows_value, uint32_t* err) {
   using C = QCfg<MB>;
   constexpr int kQXStages = C::kXStages, kQWStages = C::kWStages;
   constexpr uint32_t kQTmemCols = C::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
-  const int M = *d_rows;
+  const int M = d_rows ? *d_rows : rows_value;
   const int m0 = blockIdx.y * 128 * MB;
   if (m0 >= M) return;  // uniform over the CTA
   const int tile = blockIdx.x;
@@ -241,6 +241,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
             }
           }
         }
+      } else if (mode == kSkinnyF32) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t v32[32];
+          dev::tmem_ld_32x32b_x32(base + c, v32);
+          dev::tc_wait_ld();
+          if (row < M) {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<float*>(y) + (size_t)row * ldy + tile * 128 + c);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) dst[v] = make_uint4(v32[4 * v], v32[4 * v + 1], v32[4 * v + 2], v32[4 * v + 3]);
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
@@ -291,7 +303,8 @@ cudaError_t launch_mb(const CUtensorMap* map_x, const uint8_t* packed, const Ski
     configured[dev] = true;
   }
   dim3 grid(n_tiles, (max_rows + 128 * MB - 1) / (128 * MB));
-  gemm_q_kernel<MB><<<grid, kQThreads, smem, s>>>(*map_x, packed, tiles, slabs, chunk_max, mode, y, ldy, d_rows, err);
+  gemm_q_kernel<MB><<<grid, kQThreads, smem, s>>>(*map_x, packed, tiles, slabs, chunk_max, mode, y, ldy, d_rows,
+                                                   max_rows, err);
   return cudaGetLastError();
 }
 }  // namespace
@@ -301,7 +314,8 @@ cudaError_t launch_mb(const CUtensorMap* map_x, const uint8_t* packed, const Ski
 cudaError_t launch_gemm_q(const CUtensorMap* map_x, const uint8_t* packed, const SkinnyTile* tiles, int n_tiles,
                           int slabs, int chunk_max, int mode, __half* y, int ldy, const int* d_rows, int max_rows,
                           uint32_t* err, cudaStream_t s) {
-  if (n_tiles < 1 || slabs < 1 || chunk_max < 1 || max_rows < 1 || (mode != kSkinnyPlain && mode != kSkinnySwiglu))
+  if (n_tiles < 1 || slabs < 1 || chunk_max < 1 || max_rows < 1 ||
+      (mode != kSkinnyPlain && mode != kSkinnySwiglu && mode != kSkinnyF32))
     return cudaErrorInvalidValue;
   if ((long long)n_tiles * ((max_rows + 511) / 512) >= 2 * 148)
     return launch_mb<4>(map_x, packed, tiles, n_tiles, slabs, chunk_max, mode, y, ldy, d_rows, max_rows, err, s);

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(192, 1)
   // ---- split-K reduction over the cluster + fused epilogue ----
   dev::cluster_sync();
   {
-    const int T = min(*a.d_tokens, NP);
+    const int T = min(a.d_tokens ? *a.d_tokens : a.tokens, NP);
     const int S = a.splits, rank = split, n0 = tile * 128;
     const uint32_t red_addr = dev::smem_u32(raw);
     auto sum_row = [&](int t, int r) -> float {
@@ -217,11 +217,12 @@ __global__ void __launch_bounds__(192, 1)
         if (i < S) acc = __fadd_rn(acc, v[i]);
       return acc;
     };
-    if (a.mode == kSkinnyPlain) {
+    if (a.mode == kSkinnyPlain || a.mode == kSkinnyF32) {
       const int r0 = rank * 128 / S, nr = (rank + 1) * 128 / S - r0;
       for (int it = threadIdx.x; it < nr * T; it += blockDim.x) {
         const int r = r0 + it % nr, t = it / nr;
-        a.out[(size_t)t * a.ldo + n0 + r] = __float2half_rn(sum_row(t, r));
+        if (a.mode == kSkinnyF32) reinterpret_cast<float*>(a.out)[(size_t)t * a.ldo + n0 + r] = sum_row(t, r);
+        else a.out[(size_t)t * a.ldo + n0 + r] = __float2half_rn(sum_row(t, r));
       }
     } else if (a.mode == kSkinnyRope) {
       const int* off = a.merged ? a.meta->tgt_off : a.meta->src_off;

@@ -84,6 +84,10 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_merge": (I, [P, P, P, I, P, P]),
         "nemo_op_pool": (I, [P, P, I, P]),
         "nemo_op_gemm": (I, [I, P, P, P, P, I, I, I, I]),
+        "nemo_op_qmatmul_image_bytes": (S, [I, I, I]),
+        "nemo_op_qmatmul_image": (I, [I, P, I, I, P]),
+        "nemo_op_qmatmul_enqueue": (I, [I, P, P, I, I, I, P, P, P]),
+        "nemo_op_qmatmul": (I, [I, P, P, I, I, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -144,6 +144,19 @@ def test_medium_sequence(models):
     compare(gpu, orc, [300, 170], seed=3)
 
 
+@pytest.mark.parametrize("length", [1500, 5000], ids=["config4_request_1x1500", "config5_request_1x5000"])
+def test_full_size_request(models, length):
+    """The 16-layer forward at the request shapes of configs 4 and 5, every
+    layer against the oracle. 1500 tokens: layers 0-3 at 1500 rows, 4-15 at
+    960, and the O / down GEMMs split K over f32 partial slots (96 output tiles
+    on 148 SMs) that the residual RMSNorm sums. 5000 tokens: every layer
+    samples every third key (1667 keys at 5000 rows, 1067 at 3200 merged)."""
+    flavour, gpu, orc = models
+    if flavour != "kquant":
+        pytest.skip("one flavour is enough at this size")
+    compare(gpu, orc, [length], seed=41)
+
+
 @pytest.mark.parametrize("lengths", [[150, 97, 64], [700] * 3, [520, 9]])
 def test_batched_dequant_fused_vs_f16_weights(models, lengths, monkeypatch):
     """NEMO_BATCHED=fused: batched plans (> 64 tokens) decode the packed blocks

@@ -36,3 +36,8 @@ def test_host_only_entry_points():
     t = np.zeros((7, 64, 2), np.float32)
     assert lib.nemo_rope_table(7, t.ctypes.data_as(ctypes.c_void_p)) == 0
     assert np.array_equal(t, oracle.rope_table(7))
+    # tile-slab image size of the standalone quantised matmul: 256-byte tile
+    # table + 128 x 256 chunks (Q4_K / Q4_0: 2 x 64 x 144 B; Q6_K: 2 x 64 x 210 B)
+    assert lib.nemo_op_qmatmul_image_bytes(0, 2048, 2048) == 256 + 16 * 8 * 18432
+    assert lib.nemo_op_qmatmul_image_bytes(1, 256, 6144) == 256 + 2 * 24 * 26880
+    assert lib.nemo_op_qmatmul_image_bytes(0, 200, 2048) == 0
