@@ -12,16 +12,22 @@
 //   * the array holds kNoAllocCompactRows sampled key rows (K and V, 8 heads x
 //     128 f16 each): 8 MiB + 256 B per GPU that loads this library, held until
 //     the process exits;
-//   * a call whose sampled rows could exceed that (rows / 3 + batch + 1 >
-//     kNoAllocCompactRows while max_len > 2048) is rejected with
-//     NEMO_ERR_ARGS before anything runs;
-//   * every call shares the one array and it keeps the last call's contents;
-//     the error word is cleared at the start of each call (the compact rows
-//     are fully rewritten before they are read); two calls that overlap on
-//     the GPU (other threads or streams) race on it;
+//   * the call reads the run's metadata back to the host (a blocking copy of a
+//     few hundred bytes, no allocation) to learn how many sampled rows it
+//     needs; a call needing more than kNoAllocCompactRows is rejected with
+//     NEMO_ERR_ARGS before any device work. Exact-attention metadata samples
+//     no keys, so such calls need none and are never rejected;
+//   * every call shares the one array and it keeps the last call's contents.
+//     Each call clears the error word, writes its sampled rows, and zeroes the
+//     rows after them up to the end of the last 128-row tile the attention
+//     kernel loads: key weights there are 0, but a stale non-finite V value
+//     from an earlier call would still turn 0 * Inf into NaN in the P.V
+//     product. Two calls that overlap on the GPU (other threads or streams)
+//     race on the array;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress with that device current) and caches it; make that
 //     first call before any stream capture.
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/nemo_ops.h"
@@ -71,12 +77,13 @@ extern "C" int nemo_op_attention_tc_noalloc(const void* d_q, const void* d_k, co
     set_error("nemo_op_attention_tc_noalloc: bad arguments");
     return kErrArgs;
   }
-  const bool sampling = max_len > kSampleThreshold;
-  const long long need = (long long)rows / kSampleStride + batch + 1;
-  if (sampling && need > kNoAllocCompactRows) {
-    set_error("nemo_op_attention_tc_noalloc: up to " + std::to_string(need) +
-              " sampled key rows needed, the fixed scratch holds " + std::to_string(kNoAllocCompactRows) +
-              " (rows / 3 + batch + 1 must not exceed it when max_len > 2048)");
+  Meta hm;
+  NEMO_CUDA_TRY(cudaMemcpy(&hm, d_meta, sizeof(Meta), cudaMemcpyDeviceToHost));
+  const int nb = hm.batch < 0 ? 0 : hm.batch > kMaxBatch ? kMaxBatch : hm.batch;
+  const long long need = hm.samp_off[merged ? 1 : 0][nb];
+  if (need < 0 || need > kNoAllocCompactRows) {
+    set_error("nemo_op_attention_tc_noalloc: " + std::to_string(need) +
+              " sampled key rows needed, the fixed scratch holds " + std::to_string(kNoAllocCompactRows));
     return kErrArgs;
   }
   uint8_t* base = nullptr;
@@ -91,9 +98,16 @@ extern "C" int nemo_op_attention_tc_noalloc(const void* d_q, const void* d_k, co
       make_tmap_f16(&maps.vc, vc, kKVWidth, kNoAllocCompactRows, 64, 128))
     return kErrCuda;
   NEMO_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(uint32_t), 0));
-  if (sampling) {
+  if (need > 0) {
     NEMO_CUDA_TRY(launch_gather_sampled((const __half*)d_k, (const __half*)d_qkv, (const Meta*)d_meta, merged != 0,
                                         (int)need, kc, vc, 0));
+    // rows past the sampled ones that the last 128-row K/V tile still loads
+    const long long tail = std::min<long long>((need + 127) / 128 * 128, kNoAllocCompactRows);
+    if (tail > need) {
+      const size_t off = (size_t)need * kKVWidth, len = (size_t)(tail - need) * kKVWidth * sizeof(__half);
+      NEMO_CUDA_TRY(cudaMemsetAsync(kc + off, 0, len, 0));
+      NEMO_CUDA_TRY(cudaMemsetAsync(vc + off, 0, len, 0));
+    }
   }
   NEMO_CUDA_TRY(launch_attention_tc(maps, (const Meta*)d_meta, merged != 0, batch, max_len, (__half*)d_out, err, 0));
   uint32_t h = 0;
