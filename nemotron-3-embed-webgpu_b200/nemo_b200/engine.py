@@ -20,6 +20,21 @@ import math
 import numpy as np
 
 
+def micro_batches(lengths: list[int], max_batch_size: int = 16) -> list[list[int]]:
+    """The engine's split of a queue of requests (token counts, BOS included)
+    into micro-batches, as ``_flush`` takes them with no storage cap (the B200
+    runtime has none): up to ``max_batch_size`` per batch, at most 8 when the
+    longest candidate has >= 1500 tokens (embedding-engine.ts:62-69). Returns
+    lists of request indices in queue order."""
+    out, i = [], 0
+    while i < len(lengths):
+        candidates = lengths[i:i + max_batch_size]
+        take = min(max_batch_size, 8 if max(candidates) >= 1500 else max_batch_size)
+        out.append(list(range(i, min(i + take, len(lengths)))))
+        i += take
+    return out
+
+
 class NemotronEmbeddingEngine:
     def __init__(self, runtime, tokenizer, max_batch_size: int = 16, batch_window_ms: float = 0,
                  bos_token: int = 1, pad_token: int = 11):

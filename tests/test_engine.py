@@ -121,3 +121,33 @@ def test_long_requests_cap_at_eight_and_failures_reject_the_batch():
 def test_rejects_bad_batch_size():
     with pytest.raises(ValueError):
         NemotronEmbeddingEngine(object(), lambda t: None, 17)
+
+
+def test_micro_batches_follow_the_engines_flush():
+    """micro_batches (the bench's split of a request queue) takes the same
+    batches as the engine's flush: <= 16, <= 8 when the longest candidate has
+    >= 1500 tokens."""
+    from nemo_b200.engine import micro_batches
+    assert micro_batches([15] * 16) == [list(range(16))]
+    assert micro_batches([1500] * 16) == [list(range(8)), list(range(8, 16))]
+    assert micro_batches([5000] * 10) == [list(range(8)), [8, 9]]
+    assert micro_batches([15] * 20) == [list(range(16)), [16, 17, 18, 19]]
+    assert micro_batches([10, 1499, 1500, 3]) == [[0, 1, 2, 3]]  # one candidate >= 1500 caps at 8
+    sizes = []
+
+    class Runtime:
+        def create_plan(self, batch, sequence):
+            class Plan:
+                def run(self, ids, lengths):
+                    sizes.append(batch)
+                    return [np.zeros(1, np.float32) for _ in range(batch)]
+            return Plan()
+
+    lengths = [20] * 3 + [1600] * 9 + [7] * 20
+    engine = NemotronEmbeddingEngine(Runtime(), _Tok(lambda t: [[1] * int(t)]), 16, 0, 1)
+
+    async def main():
+        return await asyncio.gather(*[engine.embed(str(n)) for n in lengths])
+
+    asyncio.run(main())
+    assert sizes == [len(b) for b in micro_batches(lengths)]
