@@ -50,13 +50,13 @@ constexpr int kRawStages = 4;   // packed weight chunks in shared memory
 constexpr int kASlabs = 3;     // decoded A slabs in TMEM (128 x 256 f16 = 128 columns each)
 constexpr int kXStages = 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint64_t kLimitNs = 2000000000ull;
 constexpr uint32_t kDevErrGridBarrier = 4u;
 
 __device__ __forceinline__ uint32_t ld_err(const uint32_t* e) { return *reinterpret_cast<const volatile uint32_t*>(e); }
 
-// Bounded mbarrier wait that also returns false once the error word is set.
-__device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* err) {
+// Bounded mbarrier wait (limit_ns) that also returns false once the error
+// word is set.
+__device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* err, uint64_t limit_ns) {
   if (dev::mbar_try_wait(bar, parity)) return true;
   if (ld_err(err)) return false;
   const uint64_t t0 = dev::globaltimer();
@@ -64,7 +64,7 @@ __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t* er
     if (dev::mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (ld_err(err)) return false;
-      if (dev::globaltimer() - t0 > kLimitNs) {
+      if (dev::globaltimer() - t0 > limit_ns) {
         atomicOr(err, kDevErrMbarTimeout);
         return false;
       }
@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   const int seg0 = a.seg_start[cta];
   const int nseg = a.seg_start[cta + 1] - seg0;
   uint32_t* err = a.err;
+  const uint64_t lim = a.wait_ns;  // bound of every wait (2 s unless a test shortens it)
   {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.segs + seg0);
     uint32_t* dst = reinterpret_cast<uint32_t*>(segs);
@@ -244,10 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
         if (*reinterpret_cast<volatile int*>(&sh->quiet)) {
           const uint64_t t0 = dev::globaltimer();
-          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < kLimitNs) __nanosleep(128);
+          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < lim) __nanosleep(128);
         }
         const int s = it % kRawStages;
-        if (!__all_sync(0xffffffffu, wait(rempty + 8 * s, ((it / kRawStages) & 1) ^ 1, err))) {
+        if (!__all_sync(0xffffffffu, wait(rempty + 8 * s, ((it / kRawStages) & 1) ^ 1, err, lim))) {
           ok = false;
           break;
         }
@@ -272,12 +273,12 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     for (int si = 0; si < nseg && ok; ++si) {
       const FwdSeg sg = segs[si];
       const int d = si & 1;
-      if (!__all_sync(0xffffffffu, wait(dempty + 8 * d, ((si >> 1) & 1) ^ 1, err))) break;
+      if (!__all_sync(0xffffffffu, wait(dempty + 8 * d, ((si >> 1) & 1) ^ 1, err, lim))) break;
       dev::tc_fence_after();
       for (int sl = sg.s0; sl < sg.s1; ++sl, ++it) {
         const int xs = it % kXStages, s = it % kASlabs;
-        if (!__all_sync(0xffffffffu, wait(xfull + 8 * xs, (it / kXStages) & 1, err) &&
-                                         wait(afull + 8 * s, (it / kASlabs) & 1, err))) {
+        if (!__all_sync(0xffffffffu, wait(xfull + 8 * xs, (it / kXStages) & 1, err, lim) &&
+                                         wait(afull + 8 * s, (it / kASlabs) & 1, err, lim))) {
           ok = false;
           break;
         }
@@ -327,10 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         // (attention, norms); bounded like every other wait.
         if (*reinterpret_cast<volatile int*>(&sh->quiet)) {
           const uint64_t t0 = dev::globaltimer();
-          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < kLimitNs) __nanosleep(128);
+          while (*reinterpret_cast<volatile int*>(&sh->quiet) && dev::globaltimer() - t0 < lim) __nanosleep(128);
         }
         const int rs = it % kRawStages;
-        if (!__all_sync(0xffffffffu, wait(rfull + 8 * rs, (it / kRawStages) & 1, err))) {
+        if (!__all_sync(0xffffffffu, wait(rfull + 8 * rs, (it / kRawStages) & 1, err, lim))) {
           ok = false;
           break;
         }
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
         const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
         const int s = it % kASlabs;
-        if (!__all_sync(0xffffffffu, wait(aempty + 8 * s, ((it / kASlabs) & 1) ^ 1, err))) {
+        if (!__all_sync(0xffffffffu, wait(aempty + 8 * s, ((it / kASlabs) & 1) ^ 1, err, lim))) {
           ok = false;
           break;
         }
@@ -366,19 +367,23 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     const int T0 = min(meta->t0, NP), T1 = min(meta->t1, NP);
     int si = 0, xit = 0, gseg = 0, eph = 0;
     uint32_t nbar = 0;
+    // Test hook: when set, grid barrier number *test_stall (1-based) waits
+    // for one arrival more than the grid has, so it gives up at the wait
+    // bound and the whole grid unwinds through the error word.
+    const uint32_t stall = a.test_stall ? *reinterpret_cast<const volatile uint32_t*>(a.test_stall) : 0u;
 
     auto grid_barrier = [&]() {
       pw_sync();
       if (pt == 0) {
         red_add_release(&a.sync[0], 1u);
-        const uint32_t target = (++nbar) * (uint32_t)G;
+        const uint32_t target = (++nbar) * (uint32_t)G + (nbar == stall ? 1u : 0u);
         if (!ld_err(err)) {
           const uint64_t t0 = dev::globaltimer();
           for (uint32_t i = 0;; ++i) {
             if (ld_acquire(&a.sync[0]) >= target) break;
             if ((i & 15u) == 15u) {
               if (ld_err(err)) break;
-              if (dev::globaltimer() - t0 > kLimitNs) {
+              if (dev::globaltimer() - t0 > lim) {
                 atomicOr(err, kDevErrGridBarrier);
                 break;
               }
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         }
         __syncwarp();
       }
-      const bool got = wait(ebar, eph & 1, err);
+      const bool got = wait(ebar, eph & 1, err, lim);
       ++eph;
       // Each thread keeps one accumulator per token (independent chains) and
       // adds the slots in order; f16 gate and up, then SwiGLU (ops.ts:74-89).
@@ -439,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     // that completes one runs its SwiGLU epilogue (returns true).
     auto drain = [&](const FwdSeg& sg, int T, bool counted) -> bool {
       const int d = gseg & 1;
-      const bool got = __all_sync(0xffffffffu, wait(dfull + 8 * d, (gseg >> 1) & 1, err));
+      const bool got = __all_sync(0xffffffffu, wait(dfull + 8 * d, (gseg >> 1) & 1, err, lim));
       ++gseg;
       const int ss = sstride[sg.proj];
       // O / down: token-major [t][tile][slot] (a norm row reads one block);
@@ -501,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         if (pt < 32) {
           for (int sl = sg.s0; sl < sg.s1; ++sl, ++xit) {
             const int xs = xit % kXStages;
-            if (__all_sync(0xffffffffu, wait(xempty + 8 * xs, ((xit / kXStages) & 1) ^ 1, err)) && dev::elect_one()) {
+            if (__all_sync(0xffffffffu, wait(xempty + 8 * xs, ((xit / kXStages) & 1) ^ 1, err, lim)) && dev::elect_one()) {
               dev::mbar_arrive_expect_tx(xfull + 8 * xs, kXBytes);
               for (int q = 0; q < 4; ++q)
                 dev::tma_load_2d(dev::smem_u32(xring + xs * kXBytes + q * NP * 128), xmap, sl * 256 + q * 64, 0,

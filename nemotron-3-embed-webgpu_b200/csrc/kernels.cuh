@@ -175,13 +175,16 @@ struct SkinnyTile {
   uint8_t pad[6];
 };
 
-enum SkinnyMode { kSkinnyPlain = 0, kSkinnyRope = 1, kSkinnySwiglu = 2 };
+// kSkinnyF32: plain Y stored as f32 (the standalone quantised matmul entry
+// point; `out` then points at floats and ldo counts floats).
+enum SkinnyMode { kSkinnyPlain = 0, kSkinnyRope = 1, kSkinnySwiglu = 2, kSkinnyF32 = 3 };
 
 struct SkinnyArgs {
   const uint8_t* packed;
   const SkinnyTile* tiles;
   uint32_t* err;
-  const int* d_tokens;
+  const int* d_tokens;  // valid token rows (device int); null: `tokens` below
+  int tokens;
   const Meta* meta;
   int merged;
   int n, slabs, splits, slabs_max, chunk_max;
@@ -196,6 +199,9 @@ struct SkinnyArgs {
 };
 
 size_t skinny_smem_bytes(int np, int slabs_max, int chunk_max, int rstages);
+// Split-K factor and weight-ring depth of the small-T kernel for a projection
+// of `tiles` 128-row tiles and `slabs` 256-column slabs (plan.cu).
+void pick_splits(int tiles, int slabs, int np, int chunk_max, int* splits_out, int* rstages_out);
 // Grid (tiles, splits), cluster (1, splits) with splits <= 16 and <= slabs;
 // np = tokens padded to 16, 32 or 64; map_x box 64 x np.
 cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np, int tiles, cudaStream_t s);
@@ -208,6 +214,16 @@ cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np,
 cudaError_t launch_gemm_q(const CUtensorMap* map_x, const uint8_t* packed, const SkinnyTile* tiles, int n_tiles,
                           int slabs, int chunk_max, int mode, __half* y, int ldy, const int* d_rows, int max_rows,
                           uint32_t* err, cudaStream_t s);
+
+// --- standalone quantised matmul (qmatmul.cu) ------------------------------
+// Bytes of the device tile-slab image of an [n x k] matrix (0 if n is not a
+// multiple of 128 or k of 256), the device re-tile of GGUF / tile32 blocks into
+// it, and Y[m x n] f32 = X[m x k] . W^T on the image (small-token kernel for
+// m <= 64, dequant-fused GEMM above). err: device word for bounded waits.
+size_t qmatmul_image_bytes(int fmt, int n, int k);
+cudaError_t launch_qmatmul_retile(int fmt, const uint8_t* src, int n, int k, uint8_t* image, cudaStream_t s);
+int qmatmul_enqueue(int fmt, const uint8_t* image, const __half* x, int m, int n, int k, float* y, uint32_t* err,
+                    cudaStream_t s);
 
 // --- persistent single-launch forward for <= kFwdNP tokens (k_forward.cu) ---
 constexpr int kFwdNP = 16;        // token rows per projection (padded)
@@ -255,6 +271,9 @@ struct FwdArgs {
   int n_layers;
   int chunk_max;
   int exact;                // no merge, pool over the unmerged rows
+  uint64_t wait_ns;          // bound of every wait in the kernel (2 s; tests shorten it)
+  const uint32_t* test_stall;  // test hook (null in normal plans): grid barrier number
+                               // *test_stall (1-based, 0 = none) can never complete
 };
 
 size_t forward_smem_bytes(int chunk_max, int scratch_slots, int max_segs, int n_layers);

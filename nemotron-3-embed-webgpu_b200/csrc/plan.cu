@@ -11,7 +11,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <chrono>
 #include <numeric>
+#include <thread>
 
 #include "runtime.h"
 
@@ -36,17 +38,6 @@ struct Dump {
   int* tokens = nullptr;
   size_t stride = 0;
 };
-
-namespace {
-
-int pick_bn(int rows, int n) {
-  const int mt = (rows + kGemmTileM - 1) / kGemmTileM;
-  if ((long long)mt * (n / 256) >= 148) return 2;
-  if ((long long)mt * (n / 128) >= 148) return 1;
-  return 0;
-}
-
-int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 // Split-K factor and weight-ring depth of the small-T kernel. The splits of a
 // tile form one cluster (at most 16 CTAs) and each needs >= 1 slab. Among the
@@ -75,6 +66,35 @@ void pick_splits(int tiles, int slabs, int np, int chunk_max, int* splits_out, i
       }
     }
 }
+
+namespace {
+
+int env_int(const char* name, int fallback) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : fallback;
+}
+
+// Bound of every wait inside the single-launch forward: 2 s, or shorter for a
+// test that makes one run out (NEMO_TEST_WAIT_LIMIT_MS at plan creation).
+int test_wait_limit_ms() { return std::min(2000, std::max(1, env_int("NEMO_TEST_WAIT_LIMIT_MS", 2000))); }
+
+// Before each run of a plan created with NEMO_TEST_FAULTS set: the grid
+// barrier the next run stalls at (NEMO_TEST_STALL_BARRIER, 0 = none).
+int stage_test_stall(DevicePlan& p) {
+  if (!p.test_stall) return kOk;
+  *p.h_test_stall = (uint32_t)std::max(0, env_int("NEMO_TEST_STALL_BARRIER", 0));
+  NEMO_CUDA_TRY(cudaMemcpyAsync(p.test_stall, p.h_test_stall, 4, cudaMemcpyHostToDevice, p.stream));
+  return kOk;
+}
+
+int pick_bn(int rows, int n) {
+  const int mt = (rows + kGemmTileM - 1) / kGemmTileM;
+  if ((long long)mt * (n / 256) >= 148) return 2;
+  if ((long long)mt * (n / 128) >= 148) return 1;
+  return 0;
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 template <typename T>
 int plan_alloc(DevicePlan& p, T** ptr, size_t bytes) {
@@ -225,6 +245,8 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   a.n_layers = L;
   a.chunk_max = chunk_max;
   a.exact = p.exact ? 1 : 0;
+  a.wait_ns = (uint64_t)test_wait_limit_ms() * 1000000ull;
+  a.test_stall = p.test_stall;
   // X operands by TMA; the small-T maps (box 64 x 16) exist because tmax0 <= 16.
   a.xmap[0] = p.xmap_norm[0];
   a.xmap[1] = p.xmap_norm[1];
@@ -243,6 +265,7 @@ void free_device_plan(DevicePlan& p) {
   if (p.h_lengths) cudaFreeHost(p.h_lengths);
   if (p.h_out) cudaFreeHost(p.h_out);
   if (p.h_err) cudaFreeHost(p.h_err);
+  if (p.h_test_stall) cudaFreeHost(p.h_test_stall);
   if (p.stream) cudaStreamDestroy(p.stream);
   p = DevicePlan();
 }
@@ -573,6 +596,11 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, b
 
   // The lengths buffer must hold a valid run before the first launch.
   NEMO_CUDA_TRY(cudaMemcpy(p.lengths, p.h_lengths, (size_t)(cap_batch + 1) * 4, cudaMemcpyHostToDevice));
+  if (env_int("NEMO_TEST_FAULTS", 0)) {
+    if (plan_alloc(p, &p.test_stall, 4)) return kErrCuda;
+    NEMO_CUDA_TRY(cudaMallocHost(&p.h_test_stall, 4));
+    *p.h_test_stall = 0;
+  }
   if (int rc = setup_forward(m, dm, p)) return rc;
   if (int rc = capture(p, m->n_layers, true, &p.graph_host)) return rc;
   if (int rc = capture(p, m->n_layers, false, &p.graph_device)) return rc;
@@ -619,6 +647,8 @@ int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, uint32_t flags, nem
   plan->batch = (int)batch;
   plan->seq = (int)seq;
   plan->exact = (flags & 1u) != 0;
+  plan->host_deadline_ns = (int64_t)std::max(1, env_int("NEMO_HOST_DEADLINE_MS", 60000)) * 1000000ll;
+  plan->fail_device = env_int("NEMO_TEST_FAIL_DEVICE", -1);
   for (auto& dm : m->devs) {
     auto dp = std::make_unique<DevicePlan>();
     int rc = create_device_plan(m, dm.get(), (int)batch, (int)seq, plan->exact, *dp);
@@ -688,6 +718,31 @@ int validate_inputs(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const ui
   return kOk;
 }
 
+// Waits for the device's stream with a host-side deadline: polls the stream
+// instead of blocking in cudaStreamSynchronize, so a caller never waits longer
+// than the plan's deadline (the device-side waits are bounded as well).
+int wait_stream(DevicePlan& d, int64_t deadline_ns) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t i = 0;; ++i) {
+    const cudaError_t e = cudaStreamQuery(d.stream);
+    if (e == cudaSuccess) return kOk;
+    if (e != cudaErrorNotReady) {
+      set_error(std::string("CUDA error: ") + cudaGetErrorString(e) + " while waiting for device " +
+                std::to_string(d.device));
+      return kErrCuda;
+    }
+    if ((i & 63u) == 63u) {
+      if (std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count() >
+          deadline_ns) {
+        set_error("host deadline of " + std::to_string(deadline_ns / 1000000) + " ms passed waiting for device " +
+                  std::to_string(d.device));
+        return kErrTimeout;
+      }
+      std::this_thread::yield();
+    }
+  }
+}
+
 int check_err(DevicePlan& d) {
   if (*d.h_err) {
     set_error("a device-side bounded wait timed out (error word " + std::to_string(*d.h_err) + ")");
@@ -723,28 +778,49 @@ int plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t*
       load[d] += lengths[r];
     }
   }
+  // A failure on any device rejects the whole micro-batch (the caller's
+  // engine rejects every request of it, embedding-engine.ts:84-89); the other
+  // devices' work is still waited for, so nothing is in flight on return.
+  int rc = kOk;
+  std::vector<bool> launched(ndev, false);
   for (int d = 0; d < ndev; ++d) {
     DevicePlan& p = *plan->devs[d];
     if (assign[d].empty()) continue;
+    if (d == plan->fail_device) {
+      set_error("injected failure of device " + std::to_string(p.device) + "'s share (NEMO_TEST_FAIL_DEVICE)");
+      rc = kErrCuda;
+      continue;
+    }
     for (size_t j = 0; j < assign[d].size(); ++j) {
       const int r = assign[d][j];
       memcpy(p.h_ids + j * p.seq, ids + (size_t)r * plan->seq, (size_t)plan->seq * 4);
       p.h_lengths[j] = lengths[r];
     }
     p.h_lengths[p.cap_batch] = (uint32_t)assign[d].size();
-    NEMO_CUDA_TRY(cudaSetDevice(p.device));
-    NEMO_CUDA_TRY(cudaGraphLaunch(p.graph_host, p.stream));
+    cudaError_t e = cudaSetDevice(p.device);
+    if (e == cudaSuccess && stage_test_stall(p) != kOk) e = cudaErrorUnknown;
+    if (e == cudaSuccess) e = cudaGraphLaunch(p.graph_host, p.stream);
+    if (e != cudaSuccess) {
+      set_error(std::string("CUDA error: ") + cudaGetErrorString(e) + " launching device " + std::to_string(p.device));
+      rc = kErrCuda;
+      continue;
+    }
+    launched[d] = true;
   }
-  int rc = kOk;
+  const std::string first_error = rc ? last_error() : "";
   for (int d = 0; d < ndev; ++d) {
     DevicePlan& p = *plan->devs[d];
-    if (assign[d].empty()) continue;
-    NEMO_CUDA_TRY(cudaSetDevice(p.device));
-    NEMO_CUDA_TRY(cudaStreamSynchronize(p.stream));
-    if (int e = check_err(p)) rc = e;
+    if (!launched[d]) continue;
+    int e = cudaSetDevice(p.device) == cudaSuccess ? wait_stream(p, plan->host_deadline_ns) : kErrCuda;
+    if (!e) e = check_err(p);
+    if (e) {
+      if (!rc) rc = e;
+      continue;
+    }
     for (size_t j = 0; j < assign[d].size(); ++j)
       memcpy(out + (size_t)assign[d][j] * kHidden, p.h_out + j * kHidden, kHidden * 4);
   }
+  if (!first_error.empty()) set_error(first_error);
   return rc;
 }
 
@@ -764,6 +840,7 @@ int plan_run_device(nemo_plan* plan, const uint32_t* d_ids, const uint32_t* d_le
   NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths, d_lengths, (size_t)p.cap_batch * 4, cudaMemcpyDeviceToDevice, p.stream));
   NEMO_CUDA_TRY(cudaMemcpyAsync(p.lengths + p.cap_batch, p.h_lengths + p.cap_batch, 4, cudaMemcpyHostToDevice,
                                 p.stream));
+  if (int rc = stage_test_stall(p)) return rc;
   NEMO_CUDA_TRY(cudaGraphLaunch(p.graph_device, p.stream));
   NEMO_CUDA_TRY(cudaMemcpyAsync(d_out, p.out, (size_t)p.cap_batch * kHidden * 4, cudaMemcpyDeviceToDevice, p.stream));
   return kOk;

@@ -119,6 +119,11 @@ struct DevicePlan {
   FwdArgs fargs = {};
   uint32_t* fsync = nullptr;
   size_t fsync_bytes = 0;
+  // Test hooks, off unless NEMO_TEST_FAULTS is set when the plan is created:
+  // a device word the single-launch forward reads for the grid barrier to
+  // stall (NEMO_TEST_STALL_BARRIER, read at every run) and its pinned staging.
+  uint32_t* test_stall = nullptr;
+  uint32_t* h_test_stall = nullptr;
   cudaGraphExec_t graph_host = nullptr;    // H2D inputs -> forward -> D2H output
   cudaGraphExec_t graph_device = nullptr;  // forward only
   std::vector<void*> allocations;
@@ -158,4 +163,12 @@ struct nemo_plan {
   nemo::HeadPar* hp = nullptr;
   int hp_min = 0;
   bool exact = false;  // NEMO_PLAN_EXACT_ATTENTION
+  // Host-side bound on every wait for a device's stream in nemo_plan_run
+  // (NEMO_HOST_DEADLINE_MS at creation, default 60 s): past it the call
+  // returns NEMO_ERR_TIMEOUT instead of blocking.
+  int64_t host_deadline_ns = 60000000000ll;
+  // Test hook (NEMO_TEST_FAIL_DEVICE at creation, -1 = off): the plan's device
+  // with this index fails its share of every nemo_plan_run before launching
+  // anything, so the whole micro-batch is rejected.
+  int fail_device = -1;
 };
