@@ -94,15 +94,6 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   return v;
 }
 
-// 16-byte asynchronous global -> shared copy through L2 (many in flight per
-// thread without registers), and the wait for all of this thread's copies.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dev::smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -170,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   const uint32_t afull = rempty + 8 * kRawStages, aempty = afull + 8 * kASlabs;
   const uint32_t xfull = aempty + 8 * kASlabs, xempty = xfull + 8 * kXStages;
   const uint32_t dfull = xempty + 8 * kXStages, dempty = dfull + 16, fin = dempty + 16, ebar = fin + 8;
-  Shared* sh = reinterpret_cast<Shared*>(bars + 2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6);
+  const uint32_t rowbar = ebar + 8;  // the norm phase's bulk loads
+  Shared* sh = reinterpret_cast<Shared*>(bars + 2 * kRawStages + 2 * kASlabs + 2 * kXStages + 7);
   // Run metadata copied to shared memory once: this CTA's segments, slot
   // counts and strides, the run's Meta and the RoPE rows of positions < NP.
   FwdSeg* segs = reinterpret_cast<FwdSeg*>(reinterpret_cast<uint8_t*>(sh) + ((sizeof(Shared) + 15) & ~15));
@@ -215,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     }
     dev::mbar_init(fin, 1);
     dev::mbar_init(ebar, 1);
+    dev::mbar_init(rowbar, 1);
     dev::fence_mbar_init();
     sh->flag = 0;
     sh->quiet = 0;
@@ -227,9 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   __syncthreads();
   dev::tc_fence_after();
   const uint32_t tmem = sh->tmem;
-  // TMEM columns: two D buffers (segments alternate), each four accumulators
-  // (one per 64-column substage: independent MMA chains) of NP columns, then
-  // the A slabs.
+  // TMEM columns: two D accumulators of NP columns (segments alternate; every
+  // substage of a segment accumulates into its D), then the A slabs.
   const uint32_t tm_a = tmem + 8 * NP;
 
   if (warp == 0) {
@@ -289,8 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
           for (int kk = 0; kk < 4; ++kk) {
             if (dev::elect_one()) {
               const uint64_t bd = dev::make_sw128_desc(xbase + xs * kXBytes + q * NP * 128 + kk * 32);
-              dev::tc_mma_f16_ts(tmem + (4 * d + q) * NP, tm_a + s * 128 + q * 32 + kk * 8, bd, idesc,
-                                 (sl != sg.s0 || kk != 0) ? 1u : 0u);
+              dev::tc_mma_f16_ts(tmem + d * NP, tm_a + s * 128 + q * 32 + kk * 8, bd, idesc,
+                                 (sl != sg.s0 || q != 0 || kk != 0) ? 1u : 0u);
             }
             __syncwarp();
           }
@@ -365,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int batch = min(meta->batch, kMaxBatch);
     const int T0 = min(meta->t0, NP), T1 = min(meta->t1, NP);
-    int si = 0, xit = 0, gseg = 0, eph = 0;
-    uint32_t nbar = 0;
+    int si = 0, xit = 0, gseg = 0, eph = 0, nph = 0;
+    uint32_t nbarriers = 0;
     // Test hook: when set, grid barrier number *test_stall (1-based) waits
     // for one arrival more than the grid has, so it gives up at the wait
     // bound and the whole grid unwinds through the error word.
@@ -376,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       pw_sync();
       if (pt == 0) {
         red_add_release(&a.sync[0], 1u);
-        const uint32_t target = (++nbar) * (uint32_t)G + (nbar == stall ? 1u : 0u);
+        const uint32_t target = (++nbarriers) * (uint32_t)G + (nbarriers == stall ? 1u : 0u);
         if (!ld_err(err)) {
           const uint64_t t0 = dev::globaltimer();
           for (uint32_t i = 0;; ++i) {
@@ -458,18 +450,12 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         const int row = quarter * 32 + lane;
 #pragma unroll
         for (int c0 = 0; c0 < NP; c0 += 16) {
-          uint32_t v0[16], v1[16], v2[16], v3[16];
-          const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + 4 * d * NP + c0;
-          dev::tmem_ld_32x32b_x16(base, v0);
-          dev::tmem_ld_32x32b_x16(base + NP, v1);
-          dev::tmem_ld_32x32b_x16(base + 2 * NP, v2);
-          dev::tmem_ld_32x32b_x16(base + 3 * NP, v3);
+          uint32_t v[16];
+          dev::tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + d * NP + c0, v);
           dev::tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < T)
-              __stcg(slot + (size_t)(c0 + j) * tstride + row, (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) +
-                                                      (__uint_as_float(v2[j]) + __uint_as_float(v3[j])));
+            if (c0 + j < T) __stcg(slot + (size_t)(c0 + j) * tstride + row, __uint_as_float(v[j]));
         }
       }
       dev::tc_fence_before();
@@ -530,18 +516,23 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       const bool res = rpi >= 0;
       const int sst = res ? sstride[rpi] : 0;
       if (res) {
-        const uint8_t* ns = nslots + rpi * kFwdMaxTiles;
-        (void)ns;
-        const float* src = a.part + (size_t)t * (kHidden / 128) * sst * 128 + pt * 4;
-        float* dst = stage + pt * 4;
-        const int n = (kHidden / 128) * sst * 32;  // 16-byte chunks of the row's block
-        for (int k = pt; k < n; k += 128, src += 512, dst += 512) cp_async16(dst, src);
-        // the residual row joins the same batch of copies
-        const __half* xr = x + (size_t)t * kHidden;
-        __half* xs = reinterpret_cast<__half*>(stage + (kHidden / 128) * sst * 128);
-        for (int k = pt; k < kHidden / 8; k += 128) cp_async16(xs + k * 8, xr + k * 8);
-        cp_async_wait_all();
+        // Two bulk copies (the row's contiguous slot block, then its residual
+        // row) by the elected lane of the first phase warp. The staging area's
+        // earlier generic accesses are ordered before the async-proxy writes.
+        const uint32_t slot_bytes = (uint32_t)((kHidden / 128) * sst * 512);
+        dev::fence_proxy_async_smem();
         pw_sync();
+        if (pt < 32) {
+          if (dev::elect_one()) {
+            dev::mbar_arrive_expect_tx(rowbar, slot_bytes + kHidden * 2);
+            dev::bulk_load(dev::smem_u32(stage), a.part + (size_t)t * (kHidden / 128) * sst * 128, slot_bytes, rowbar);
+            dev::bulk_load(dev::smem_u32(stage + (kHidden / 128) * sst * 128), x + (size_t)t * kHidden, kHidden * 2,
+                           rowbar);
+          }
+          __syncwarp();
+        }
+        wait(rowbar, nph & 1, err, lim);
+        ++nph;
       }
       float v[2][8];
       float ss[2] = {0.f, 0.f};
@@ -880,8 +871,9 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         o[1] = make_float4(t[h][4] * inv, t[h][5] * inv, t[h][6] * inv, t[h][7] * inv);
       }
     }
-    // The last epilogue copy has landed before the CTA may exit.
+    // The last epilogue and norm copies have landed before the CTA may exit.
     if (pt == 0 && eph > 0) dev::mbar_wait(ebar, (eph - 1) & 1, err, 100000000ull);
+    if (pt == 0 && nph > 0) dev::mbar_wait(rowbar, (nph - 1) & 1, err, 100000000ull);
     // TMA loads of X issued without a matching MMA (after an error) land too.
     if (pt == 0)
       for (int j = xit > kXStages ? xit - kXStages : 0; j < xit; ++j)
@@ -910,7 +902,7 @@ int forward_scratch_slots(int gate_up_slots, int residual_slots) {
 size_t forward_smem_bytes(int chunk_max, int scratch_slots, int max_segs, int n_layers) {
   constexpr int kXBytes = 4 * kFwdNP * 128;
   return 1024 + (size_t)kXStages * kXBytes + (size_t)scratch_slots * kFwdNP * 128 * 4 +
-         (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 6) +
+         (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 7) +
          ((sizeof(Shared) + 15) & ~15) + (size_t)max_segs * sizeof(FwdSeg) + sizeof(Meta) + 16 + kFwdNP * 128 * 4 +
          (size_t)n_layers * 4 * (4 + kFwdMaxTiles);
 }
