@@ -26,6 +26,8 @@ buffers), the roofline of its dominant kernel and, at N=1, a CPU sample:
   config4     16 requests x 1500 tokens (two engine micro-batches of 8)
   config5     1 request x 5000 tokens
   config5c16  16 requests x 5000 tokens (two engine micro-batches of 8)
+  config5hp   (N = 2, 4, 8) 1 request x 5000 tokens head-parallel over all N
+              GPUs from one process (the other ranks wait on a host barrier)
 At N > 1 the forward workloads are one fixed set of requests split across the
 ranks (every engine micro-batch's requests spread longest-first over the
 ranks; "scaling": "strong"): req/s is total requests / the slowest rank's time.
@@ -500,13 +502,29 @@ def qmatmul_workload(torch, ndist, rinfo, args) -> dict:
                                                 err.data_ptr(), sp))
 
     torch.cuda.synchronize()
-    sweep(args.warmup)
+    with torch.cuda.stream(stream):
+        sweep(1)  # first calls set the kernels' attributes (not capturable)
+    stream.synchronize()
+    # One sweep captured as a CUDA graph (64 launches chained by programmatic
+    # dependent launch): the timed region is device time, not the host's rate
+    # of issuing launches through ctypes.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        cap = torch.cuda.current_stream().cuda_stream
+        for c in range(CONFIG1_COPIES):
+            check(L.nemo_op_qmatmul_enqueue(0, images[c].data_ptr(), d_x.data_ptr(), m, n, k, d_y.data_ptr(),
+                                            err.data_ptr(), cap))
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
     stream.synchronize()
     ndist.barrier(rinfo)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    sweep(args.steps)
-    end.record(stream)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
     stream.synchronize()
     ms = ndist.max_over_ranks(rinfo, start.elapsed_time(end), "cuda")
     launches = args.steps * CONFIG1_COPIES
@@ -528,7 +546,7 @@ def qmatmul_workload(torch, ndist, rinfo, args) -> dict:
         e2e_s = time.perf_counter() - t0
     e2e_s = ndist.max_over_ranks(rinfo, e2e_s, "cuda")
     ok = int(err.item()) == 0
-    del images
+    del graph, images
     return {"matmuls_per_s": rinfo.world / per_s, "unit": "matmul/s", "us_per_matmul": per_s * 1e6,
             "steps": args.steps, "matmuls_per_step": CONFIG1_COPIES, "desc": WORKLOADS["config1"]["desc"],
             "scaling": "weak", "bounded_waits_ok": ok,
@@ -540,6 +558,45 @@ def qmatmul_workload(torch, ndist, rinfo, args) -> dict:
                          "kernel": "skinny_kernel<16> (fused-dequant split-K tcgen05 projection), f32 store",
                          "algorithmic_bytes_per_matmul": CONFIG1_BYTES, "peak_source": peaks["source"] + " (copy)"},
             "gpu_launches": launches}
+
+
+def head_parallel_workload(ndist, rinfo, pack: str, args, single_req_s) -> dict | None:
+    """config5hp: one 5000-token request head-parallel over all N GPUs of the
+    box (token-sharded projections, NCCL all-to-all around attention), from
+    rank 0's process through nemo_plan_run with host buffers. The other ranks
+    wait on a host-only barrier meanwhile. Every rank takes the same barriers."""
+    from nemo_b200 import synth
+    from nemo_b200.runtime import NemotronB200Model
+    world, rank = rinfo.world, rinfo.rank
+    ndist.cpu_barrier(rinfo)
+    entry = None
+    if rank == 0:
+        model = NemotronB200Model(pack, devices=list(range(world)))
+        try:
+            reqs = synth.make_requests(args.seed, [5000])
+            ids, lens, seq = synth.pad_batch(reqs)
+            plan = model.create_plan(1, seq)
+            assert plan.head_parallel_min and plan.head_parallel_min <= 5000
+            out = np.empty((1, 2048), np.float32)
+            for _ in range(args.warmup):
+                plan.run_array(ids, lens, out)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                plan.run_array(ids, lens, out)
+            el = time.perf_counter() - t0
+            value = args.steps / el
+            entry = {"req_s": value, "unit": "req/s", "ms_per_step": el / args.steps * 1e3, "steps": args.steps,
+                     "n_devices": world, "desc": "1 request x 5000 tokens, head-parallel over all GPUs (one process)",
+                     "scaling": "strong",
+                     "timing": "host wall clock around nemo_plan_run (H2D ids, D2H embedding inside every step)",
+                     "single_device_req_s": single_req_s,
+                     "speedup_vs_single_device": (value / single_req_s) if single_req_s else None,
+                     "e2e": {"value": value, "unit": "req/s", "h2d_bytes_per_step": ids.nbytes + 4,
+                             "d2h_bytes_per_step": out.nbytes}}
+        finally:
+            model.destroy()
+    ndist.cpu_barrier(rinfo)
+    return entry
 
 
 def headline_config(name: str, args, n_layers: int, lengths: list, world: int) -> dict:
@@ -625,6 +682,13 @@ def run_ours(args) -> None:
             workloads[name] = forward_workload(torch, ndist, rinfo, model, info, name,
                                                workload_lengths(name, args.seed), True, args)
     model.destroy()
+
+    # --- one long request head-parallel over every GPU (N = 2, 4, 8) ---------
+    if world in (2, 4, 8) and (args.workloads == "all" or "config5hp" in args.workloads.split(",")):
+        single = workloads.get("config5", {}).get("req_s")
+        hp = head_parallel_workload(ndist, rinfo, pack, args, single)
+        if hp is not None:
+            workloads["config5hp"] = hp
 
     # --- CPU samples (rank 0, N = 1 only) -------------------------------------
     cpu = None

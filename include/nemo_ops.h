@@ -120,6 +120,12 @@ int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m
                             void* d_err, void* stream);
 int nemo_op_qmatmul(int fmt, const void* d_packed, const void* d_x, int m, int n, int k, void* d_y);
 
+/* Column map of the head-parallel exchange (no reference counterpart; the
+ * index function hp_pack_kernel uses, exported for layout tests without a
+ * GPU): for n_devices in {2, 4, 8}, columns[c] (c < 5120) is the QKV column
+ * that column c of the concatenated per-device send blocks carries. */
+int nemo_hp_pack_columns(int n_devices, int* columns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,22 @@ def init(backend: str, timeout_s: float = 300.0, device=None) -> RankInfo:
     return info
 
 
+_CPU_GROUP = None
+
+
+def cpu_barrier(info: RankInfo) -> None:
+    """A barrier that puts no work on any GPU (gloo over the host). Ranks wait
+    here while one rank uses every GPU of the box (head-parallel runs), so no
+    other process has a collective kernel in flight on those GPUs."""
+    global _CPU_GROUP
+    if info.world == 1:
+        return
+    import torch.distributed as dist
+    if _CPU_GROUP is None:
+        _CPU_GROUP = dist.new_group(backend="gloo")
+    dist.barrier(group=_CPU_GROUP)
+
+
 def barrier(info: RankInfo) -> None:
     if info.world > 1:
         import torch.distributed as dist

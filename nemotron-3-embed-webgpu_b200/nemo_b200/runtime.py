@@ -88,6 +88,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_qmatmul_image": (I, [I, P, I, I, P]),
         "nemo_op_qmatmul_enqueue": (I, [I, P, P, I, I, I, P, P, P]),
         "nemo_op_qmatmul": (I, [I, P, P, I, I, I, P]),
+        "nemo_hp_pack_columns": (I, [I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

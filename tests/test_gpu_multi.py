@@ -39,7 +39,8 @@ def test_head_parallel_matches_single_device(length, monkeypatch):
     """One long request on a two-device plan runs head-parallel (token-sharded
     projections, NCCL all-to-all around attention, all-gathers for the merge
     and the pool); 2300 tokens also samples every third key before the merge.
-    The embedding must match the single-device run."""
+    The embedding must match the single-device run, and the eager first run,
+    the captured second run and the replayed third run must agree bit for bit."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -54,15 +55,16 @@ def test_head_parallel_matches_single_device(length, monkeypatch):
         monkeypatch.setenv("NEMO_HEAD_PARALLEL_MIN", "512")
         plan2 = two.create_plan(1, seq)
         assert plan2.head_parallel_min == 512
-        b = plan2.run_array(ids, lens).copy()
-        b2 = plan2.run_array(ids, lens).copy()
+        b = plan2.run_array(ids, lens).copy()   # eager (sets up the NCCL peer connections)
+        b2 = plan2.run_array(ids, lens).copy()  # captured as one CUDA graph per device, then launched
+        b3 = plan2.run_array(ids, lens).copy()  # graph replay
         plan1 = one.create_plan(1, seq)
         assert plan1.head_parallel_min == 0
         a = plan1.run_array(ids, lens).copy()
     finally:
         one.destroy()
         two.destroy()
-    assert np.array_equal(b, b2)
+    assert np.array_equal(b, b2) and np.array_equal(b, b3)
     cos = float(a[0] @ b[0] / (np.linalg.norm(a[0]) * np.linalg.norm(b[0])))
     assert cos >= 0.9999, cos
     assert abs(np.linalg.norm(b[0]) - 1) < 1e-3

@@ -4,8 +4,9 @@ fewer), pack the Q/K/V columns of each head group, swap them with point-to-point
 send/recv as the grouped NCCL calls do, and must end up with the whole
 sequence of their own head group, in token order. The attention output goes
 back the same way, and the in-place all-gather of padded shards must give the
-rows in token order. Index arithmetic mirrors hp_pack_kernel /
-hp_unpack_kernel."""
+rows in token order. The pack uses the column map of hp_pack_kernel itself
+(nemo_hp_pack_columns, host-callable), checked first against the head-group
+column sets."""
 import os
 import socket
 import subprocess
@@ -41,9 +42,19 @@ WORKER = textwrap.dedent("""
     T = shard(r)
     mine = full_qkv[r * sh:r * sh + T]
 
-    def group_cols(j):  # Q, K, V columns of head group j (the pack order)
+    def expected_cols(j):  # Q, K, V columns of head group j
         return np.concatenate([np.arange(j * gq, (j + 1) * gq), QW + np.arange(j * gk, (j + 1) * gk),
                                QW + KVW + np.arange(j * gk, (j + 1) * gk)])
+
+    import ctypes
+    import sys
+    sys.path.insert(0, os.path.join(os.getcwd(), "nemotron-3-embed-webgpu_b200"))
+    from nemo_b200.runtime import check, load_library
+    cmap = np.zeros(QKVW, np.int32)
+    check(load_library().nemo_hp_pack_columns(N, cmap.ctypes.data_as(ctypes.c_void_p)))
+    for j in range(N):
+        assert np.array_equal(cmap[j * gw:(j + 1) * gw], expected_cols(j)), "pack column map"
+    group_cols = lambda j: cmap[j * gw:(j + 1) * gw]  # the map hp_pack_kernel applies
 
     # pack: block j = this shard's rows, head group j's columns
     send = [mine[:, group_cols(j)] for j in range(N)]
