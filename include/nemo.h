@@ -57,6 +57,18 @@ typedef struct {
  * f16 values on each device. devices == NULL or ndev == 0 selects device 0. */
 int nemo_model_load(const void* wgpack, size_t bytes, const int* devices, int ndev, nemo_model** out);
 
+/* Rewrites a .wgpack as a B200-tiled pack: token table and norms unchanged,
+ * every projection stored as the tile-slab image the device kernels stream,
+ * in one raw tensor blk.<l>.<fused name>.b200_tiles ([tile table][128-row x
+ * 256-column chunks]). nemo_model_load then uploads the images as they are
+ * instead of re-tiling the pack. Replaces the offline producer
+ * scripts/prepack-model.ts:28-57 for this build; the container stays WGPACK02
+ * (src/prepacked/format.ts:105-144, raw storage) with metadata
+ * "nemo.layout": "b200-tile-slab-v1". Host only (no GPU). With out == NULL
+ * only *out_bytes (the size needed) is set; otherwise capacity must be at
+ * least that size. */
+int nemo_pack_b200(const void* wgpack, size_t bytes, void* out, size_t capacity, size_t* out_bytes);
+
 /* Frees every replica. Plans of the model must be destroyed first. */
 void nemo_model_destroy(nemo_model* model);
 

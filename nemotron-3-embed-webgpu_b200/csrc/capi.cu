@@ -16,6 +16,7 @@ const char* last_error() { return g_last_error.c_str(); }
 
 int model_load(const void* data, size_t bytes, const int* devices, int ndev, nemo_model** out);
 void model_destroy(nemo_model* m);
+int pack_b200(const void* data, size_t bytes, void* out, size_t capacity, size_t* out_bytes);
 int plan_create(nemo_model* m, uint32_t batch, uint32_t seq, uint32_t flags, nemo_plan** out);
 void plan_destroy(nemo_plan* plan);
 int plan_run(nemo_plan* plan, const uint32_t* ids, size_t n_ids, const uint32_t* lengths, size_t n_lengths,
@@ -51,6 +52,10 @@ int nemo_model_load(const void* wgpack, size_t bytes, const int* devices, int nd
 }
 
 void nemo_model_destroy(nemo_model* model) { model_destroy(model); }
+
+int nemo_pack_b200(const void* wgpack, size_t bytes, void* out, size_t capacity, size_t* out_bytes) {
+  return pack_b200(wgpack, bytes, out, capacity, out_bytes);
+}
 
 int nemo_model_info_get(const nemo_model* m, nemo_model_info* info) {
   if (!m || !info) {

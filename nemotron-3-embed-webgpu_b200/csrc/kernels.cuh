@@ -225,6 +225,11 @@ cudaError_t launch_qmatmul_retile(int fmt, const uint8_t* src, int n, int k, uin
 int qmatmul_enqueue(int fmt, const uint8_t* image, const __half* x, int m, int n, int k, float* y, uint32_t* err,
                     cudaStream_t s);
 
+// Exact decode of a whole tile-slab image (device chunks + device tile table)
+// to the row-major f16 matrix [n x k]; interleave: gate/up tiles (qmatmul.cu).
+cudaError_t launch_decode_image(const uint8_t* chunks, const SkinnyTile* tiles, int ntiles, int slabs, bool interleave,
+                                int n, int k, __half* w16, cudaStream_t s);
+
 // --- persistent single-launch forward for <= kFwdNP tokens (k_forward.cu) ---
 constexpr int kFwdNP = 16;        // token rows per projection (padded)
 constexpr int kFwdMaxTiles = 96;  // 128-row tiles of the widest projection (gate/up)

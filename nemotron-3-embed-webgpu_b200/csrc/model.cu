@@ -1,9 +1,13 @@
 // Model load: parse the .wgpack, validate every tensor the forward needs,
 // upload one replica per device and decode each projection once to its
 // effective f16 weights (src/webgpu/model.ts:253-320 + the weight decode of
-// every matmul pipeline). The raw quantised bytes stay resident beside the f16
-// copy. Device memory per replica: ~0.53 GB packed + 1.74 GB f16 + 0.22 GB
-// token table, a small share of a B200's 180 GB.
+// every matmul pipeline). Each projection is kept twice: its tile-slab image
+// (the quantised blocks re-tiled for the fused-dequant kernels) and the f16
+// copy for the batched GEMM; the pack's own block layout is only a temporary
+// decode source. Device memory per replica: ~0.53 GB tile-slab + 1.74 GB f16 +
+// 0.22 GB token table, a small share of a B200's 180 GB. B200-tiled packs
+// (nemo_pack_b200) already hold the tile-slab images, so their load skips the
+// host re-tile and decodes the f16 copy from the images on the device.
 #include <string.h>
 
 #include <algorithm>
@@ -41,6 +45,46 @@ size_t expected_bytes(int fmt, int64_t rows, int64_t k) {
     case kSegQ40: return (size_t)(rows * (k / 32) * 18);
     default: return (size_t)(((rows + 31) / 32) * (k / 32) * 32 * 20);
   }
+}
+
+// B200-tiled packs (written by nemo_pack_b200) carry each projection's
+// tile-slab image as one raw tensor "blk.<l>.<fused name>.b200_tiles":
+// [SkinnyTile table of n/128 entries, padded to 256 B][chunks], chunk
+// (tile, slab) at chunks + offset + slab * chunk_bytes.
+std::string b200_name(int l, int which) { return "blk." + std::to_string(l) + "." + kFused[which] + ".b200_tiles"; }
+
+size_t b200_table_bytes(int n) { return ((size_t)(n / 128) * sizeof(SkinnyTile) + 255) / 256 * 256; }
+
+// Checks one image against the projection's shape; on success *tiles holds its table.
+int parse_b200_image(const uint8_t* bytes, uint64_t len, int which, std::vector<SkinnyTile>* tiles, int* chunk_max,
+                     const std::string& name) {
+  const int n = kProjN[which], slabs = kProjK[which] / 256, ntiles = n / 128;
+  const size_t table = b200_table_bytes(n);
+  if (len < table) {
+    set_error(name + " is shorter than its tile table");
+    return kErrFormat;
+  }
+  tiles->resize(ntiles);
+  memcpy(tiles->data(), bytes, ntiles * sizeof(SkinnyTile));
+  uint64_t expect = 0;
+  *chunk_max = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    const SkinnyTile& ti = (*tiles)[t];
+    auto region = [](int f) { return f == kSegQ6K ? 64 * 210 : 64 * 144; };
+    if (ti.fmt[0] > kSegQ40 || ti.fmt[1] > kSegQ40 || ti.offset != expect ||
+        ti.chunk_bytes != (uint32_t)(region(ti.fmt[0]) + region(ti.fmt[1]))) {
+      set_error(name + " has an inconsistent tile table (tile " + std::to_string(t) + ")");
+      return kErrFormat;
+    }
+    expect += (uint64_t)ti.chunk_bytes * slabs;
+    *chunk_max = std::max(*chunk_max, (int)ti.chunk_bytes);
+  }
+  if (table + expect != len) {
+    set_error(name + " has " + std::to_string(len) + " bytes; its tile table describes " +
+              std::to_string(table + expect));
+    return kErrFormat;
+  }
+  return kOk;
 }
 
 template <typename T>
@@ -189,18 +233,44 @@ int upload_replica(const uint8_t* file, const Pack& pack, int n_layers, int voca
   }
   if (norm("output_norm.weight", &dm.output_norm)) return kErrCuda;
 
+  const bool b200 = pack.tensors.count(b200_name(0, 0)) != 0;
   for (int l = 0; l < n_layers; ++l) {
     for (int which = 0; which < 4; ++which) {
+      Projection& pr = dm.proj[l][which];
+      pr.n = kProjN[which];
+      pr.k = kProjK[which];
+      if (dev_alloc(dm, &pr.w16, (size_t)pr.n * pr.k * 2)) return kErrCuda;
+      if (b200) {
+        // the pack holds the device layout: upload it and decode the f16 weights from it
+        const PackTensor& t = pack.tensors.at(b200_name(l, which));
+        std::vector<SkinnyTile> tiles;
+        int chunk_max = 0;
+        if (int rc = parse_b200_image(file + t.byte_offset, t.byte_length, which, &tiles, &chunk_max, t.name)) return rc;
+        const size_t table = b200_table_bytes(pr.n);
+        pr.tiles = (int)tiles.size();
+        pr.slabs = pr.k / 256;
+        pr.chunk_max = chunk_max;
+        pr.packed_bytes = t.byte_length - table;
+        if (dev_alloc(dm, &pr.packed, pr.packed_bytes) || dev_alloc(dm, &pr.d_tiles, tiles.size() * sizeof(SkinnyTile)))
+          return kErrCuda;
+        NEMO_CUDA_TRY(cudaMemcpy(pr.packed, file + t.byte_offset + table, pr.packed_bytes, cudaMemcpyHostToDevice));
+        NEMO_CUDA_TRY(cudaMemcpy(pr.d_tiles, tiles.data(), tiles.size() * sizeof(SkinnyTile), cudaMemcpyHostToDevice));
+        NEMO_CUDA_TRY(launch_decode_image(pr.packed, pr.d_tiles, pr.tiles, pr.slabs, which == kProjGateUp, pr.n, pr.k,
+                                          pr.w16, 0));
+        if (count) {
+          m->kquant++;
+          m->packed_bytes += pr.packed_bytes;
+        }
+        for (int b = 0; b < kNumBn; ++b)
+          if (int rc = make_tmap_f16(&pr.map[b], pr.w16, (uint64_t)pr.k, (uint64_t)pr.n, 64, kBnChoices[b])) return rc;
+        continue;
+      }
       std::vector<PartSpec> parts;
       std::string err;
       if (resolve(pack, l, which, &parts, &err)) {
         set_error(err);
         return kErrFormat;
       }
-      Projection& pr = dm.proj[l][which];
-      pr.n = kProjN[which];
-      pr.k = kProjK[which];
-      if (dev_alloc(dm, &pr.w16, (size_t)pr.n * pr.k * 2)) return kErrCuda;
       int row0 = 0;
       for (const PartSpec& ps : parts) {
         Segment sg;
@@ -208,9 +278,17 @@ int upload_replica(const uint8_t* file, const Pack& pack, int n_layers, int voca
         sg.row0 = row0;
         sg.rows = (int)ps.t->dims[1];
         sg.bytes = ps.t->byte_length;
-        if (dev_alloc(dm, &sg.raw, sg.bytes)) return kErrCuda;
-        NEMO_CUDA_TRY(cudaMemcpy(sg.raw, file + ps.t->byte_offset, sg.bytes, cudaMemcpyHostToDevice));
-        NEMO_CUDA_TRY(launch_decode(sg.fmt, sg.raw, sg.rows, pr.k, pr.w16 + (size_t)row0 * pr.k, nullptr, 0));
+        // the pack's blocks only feed the decode: a temporary device copy
+        uint8_t* raw = nullptr;
+        NEMO_CUDA_TRY(cudaMalloc(&raw, sg.bytes));
+        cudaError_t e = cudaMemcpy(raw, file + ps.t->byte_offset, sg.bytes, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = launch_decode(sg.fmt, raw, sg.rows, pr.k, pr.w16 + (size_t)row0 * pr.k, nullptr, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaFree(raw);
+        if (e != cudaSuccess) {
+          set_error(std::string("CUDA error: ") + cudaGetErrorString(e) + " decoding " + ps.t->name);
+          return kErrCuda;
+        }
         if (count) {
           if (sg.fmt == kSegQ40Tile32) m->compact++;
           else m->kquant++;
@@ -270,10 +348,22 @@ int validate(const Pack& pack, int* n_layers, int* vocab) {
     }
     return true;
   };
+  const bool b200 = pack.tensors.count(b200_name(0, 0)) != 0;
   for (int l = 0; l < layers; ++l) {
     if (!check_norm("blk." + std::to_string(l) + ".attn_norm.weight")) return kErrFormat;
     if (!check_norm("blk." + std::to_string(l) + ".ffn_norm.weight")) return kErrFormat;
-    for (int which = 0; which < 4; ++which) {
+    for (int which = 0; which < 4 && b200; ++which) {
+      auto it = pack.tensors.find(b200_name(l, which));
+      if (it == pack.tensors.end()) {
+        set_error("missing tensor " + b200_name(l, which));
+        return kErrFormat;
+      }
+      if (it->second.compact || it->second.dims.size() != 1 || (uint64_t)it->second.dims[0] != it->second.byte_length) {
+        set_error(it->first + " must be a raw byte tensor [bytes]");
+        return kErrFormat;
+      }
+    }
+    for (int which = 0; which < 4 && !b200; ++which) {
       std::vector<PartSpec> parts;
       std::string err;
       if (resolve(pack, l, which, &parts, &err)) {
@@ -350,7 +440,8 @@ int model_load(const void* data, size_t bytes, const int* devices, int ndev, nem
   // to every replica.
   const uint8_t* file = reinterpret_cast<const uint8_t*>(data);
   std::vector<TileSlabImage> images((size_t)n_layers * 4);
-  for (int l = 0; l < n_layers; ++l)
+  const bool b200 = pack.tensors.count(b200_name(0, 0)) != 0;
+  for (int l = 0; l < n_layers && !b200; ++l)
     for (int which = 0; which < 4; ++which) {
       std::vector<PartSpec> parts;
       std::string perr;
@@ -378,6 +469,108 @@ int model_load(const void* data, size_t bytes, const int* devices, int ndev, nem
     }
   }
   *out = m;
+  return kOk;
+}
+
+// Writes a B200-tiled pack: the input's token table and norms unchanged, and
+// every projection as its tile-slab image in one raw tensor
+// (blk.<l>.<fused name>.b200_tiles). The container stays WGPACK02 with the
+// reference's header fields (src/prepacked/format.ts:105-144), so its parser
+// still accepts the file (raw storage); metadata "nemo.layout" names the
+// layout. With out == NULL only *out_bytes is set.
+int pack_b200(const void* data, size_t bytes, void* out, size_t capacity, size_t* out_bytes) {
+  if (!data || !out_bytes) {
+    set_error("nemo_pack_b200: null argument");
+    return kErrArgs;
+  }
+  Pack pack;
+  std::string err;
+  const uint8_t* file = reinterpret_cast<const uint8_t*>(data);
+  if (!parse_wgpack(file, bytes, &pack, &err)) {
+    set_error(err);
+    return kErrFormat;
+  }
+  if (pack.tensors.count(b200_name(0, 0))) {
+    set_error("the pack is already B200-tiled");
+    return kErrArgs;
+  }
+  int n_layers = 0, vocab = 0;
+  if (int rc = validate(pack, &n_layers, &vocab)) return rc;
+  struct OutTensor {
+    std::string name;
+    std::vector<int64_t> dims;
+    int type;
+    const uint8_t* src;
+    std::vector<uint8_t> own;
+    uint64_t len;
+  };
+  std::vector<OutTensor> outs;
+  auto keep = [&](const std::string& name) {
+    const PackTensor& t = pack.tensors.at(name);
+    outs.push_back({name, t.dims, t.type, file + t.byte_offset, {}, t.byte_length});
+  };
+  keep("token_embd.weight");
+  for (int l = 0; l < n_layers; ++l) {
+    keep("blk." + std::to_string(l) + ".attn_norm.weight");
+    keep("blk." + std::to_string(l) + ".ffn_norm.weight");
+  }
+  keep("output_norm.weight");
+  for (int l = 0; l < n_layers; ++l)
+    for (int which = 0; which < 4; ++which) {
+      std::vector<PartSpec> parts;
+      if (resolve(pack, l, which, &parts, &err)) {
+        set_error(err);
+        return kErrFormat;
+      }
+      TileSlabImage img;
+      if (int rc = build_tile_slab(file, parts, kProjN[which], kProjK[which], which == kProjGateUp, &img)) return rc;
+      OutTensor o;
+      o.name = b200_name(l, which);
+      o.type = parts[0].t->type;
+      o.src = nullptr;
+      const size_t table = b200_table_bytes(kProjN[which]);
+      o.own.assign(table + img.bytes.size(), 0);
+      memcpy(o.own.data(), img.tiles.data(), img.tiles.size() * sizeof(SkinnyTile));
+      memcpy(o.own.data() + table, img.bytes.data(), img.bytes.size());
+      o.len = o.own.size();
+      o.dims = {(int64_t)o.len};
+      outs.push_back(std::move(o));
+    }
+  auto align = [](uint64_t v, uint64_t a) { return (v + a - 1) / a * a; };
+  std::string hdr = "{\"version\":2,\"sourceSha256\":\"" + pack.source_sha256 + "\",\"sourceBytes\":" +
+                    std::to_string(bytes) +
+                    ",\"layout\":\"q4_0-tile32-compact-v2\",\"tileRows\":32,\"blockValues\":32,\"blockBytes\":20,"
+                    "\"metadata\":{\"nemo.layout\":\"b200-tile-slab-v1\"},\"tensors\":[";
+  std::vector<uint64_t> offs;
+  uint64_t rel = 0;
+  for (size_t i = 0; i < outs.size(); ++i) {
+    rel = align(rel, 256);
+    offs.push_back(rel);
+    std::string dims;
+    for (size_t d = 0; d < outs[i].dims.size(); ++d) dims += (d ? "," : "") + std::to_string(outs[i].dims[d]);
+    hdr += std::string(i ? "," : "") + "{\"name\":\"" + outs[i].name + "\",\"dimensions\":[" + dims +
+           "],\"type\":" + std::to_string(outs[i].type) + ",\"storage\":\"raw\",\"offset\":" + std::to_string(rel) +
+           ",\"byteLength\":" + std::to_string(outs[i].len) + "}";
+    rel += outs[i].len;
+  }
+  hdr += "]}";
+  const uint64_t data_offset = align(12 + hdr.size(), 256);
+  const uint64_t total = data_offset + rel;
+  *out_bytes = (size_t)total;
+  if (!out) return kOk;
+  if (capacity < total) {
+    set_error("nemo_pack_b200: output buffer holds " + std::to_string(capacity) + " bytes; " + std::to_string(total) +
+              " needed");
+    return kErrArgs;
+  }
+  uint8_t* o = reinterpret_cast<uint8_t*>(out);
+  memset(o, 0, total);
+  memcpy(o, "WGPACK02", 8);
+  const uint32_t hl = (uint32_t)hdr.size();
+  memcpy(o + 8, &hl, 4);  // little-endian host
+  memcpy(o + 12, hdr.data(), hdr.size());
+  for (size_t i = 0; i < outs.size(); ++i)
+    memcpy(o + data_offset + offs[i], outs[i].own.empty() ? outs[i].src : outs[i].own.data(), outs[i].len);
   return kOk;
 }
 

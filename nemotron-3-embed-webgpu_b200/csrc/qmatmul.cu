@@ -14,7 +14,10 @@
 // batched dequant-fused GEMM (k_gemm_q.cu) above, both with f32 stores.
 //
 // Image: [SkinnyTile table of n/128 entries, padded to 256 B][chunks].
+#include <algorithm>
+
 #include "runtime.h"
+#include "tile_decode.cuh"
 
 namespace nemo {
 namespace {
@@ -77,7 +80,46 @@ __global__ void retile_kernel(int fmt, const uint8_t* __restrict__ src, int n, i
   }
 }
 
+// Writes each finished 16-byte chunk c of a decoded quarter (values 8c..8c+7)
+// to a row-major f16 matrix row.
+struct GlobalRowSink {
+  __half* row;  // first column of the quarter
+  __device__ __forceinline__ void operator()(int c, uint4 v) const { *reinterpret_cast<uint4*>(row + 8 * c) = v; }
+};
+
+// Thread per (tile, slab, row, quarter): the exact decode of one 64-value
+// quarter of one row of a tile-slab image into the row-major f16 matrix
+// (gate/up tiles: rows 0-63 are gate rows 64t.., rows 64-127 up rows n/2 + 64t..).
+__global__ void decode_image_kernel(const uint8_t* __restrict__ chunks, const SkinnyTile* __restrict__ tiles,
+                                    int ntiles, int slabs, int interleave, int n, int k, __half* __restrict__ w16) {
+  using namespace tsd;
+  const long long total = (long long)ntiles * slabs * 512;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(i & 3), row = (int)((i >> 2) & 127);
+    const long long ts = i >> 9;
+    const int slab = (int)(ts % slabs), tile = (int)(ts / slabs);
+    const SkinnyTile ti = tiles[tile];
+    const int half = row >> 6, rr = row & 63, fmt = ti.fmt[half];
+    const uint8_t* region = chunks + ti.offset + (size_t)slab * ti.chunk_bytes + (half ? region_bytes(ti.fmt[0]) : 0);
+    const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
+    const int mrow = interleave ? (half ? n / 2 + tile * 64 + rr : tile * 64 + rr) : tile * 128 + row;
+    const GlobalRowSink sink{w16 + (size_t)mrow * k + slab * 256 + q * 64};
+    if (fmt == kSegQ4K) decode_q4k(blk, q, sink);
+    else if (fmt == kSegQ6K) decode_q6k(blk, half_at(region + 64 * 208 + rr * 2), q, sink);
+    else decode_q40(blk, q, sink);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_decode_image(const uint8_t* chunks, const SkinnyTile* tiles, int ntiles, int slabs, bool interleave,
+                                int n, int k, __half* w16, cudaStream_t s) {
+  if (ntiles < 1 || slabs < 1 || n != ntiles * 128 || k != slabs * 256) return cudaErrorInvalidValue;
+  const long long total = (long long)ntiles * slabs * 512;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 148 * 16);
+  decode_image_kernel<<<blocks, 256, 0, s>>>(chunks, tiles, ntiles, slabs, interleave ? 1 : 0, n, k, w16);
+  return cudaGetLastError();
+}
 
 size_t qmatmul_image_bytes(int fmt, int n, int k) {
   if (fmt < kSegQ4K || fmt > kSegQ40Tile32 || n < 128 || n % 128 || k < 256 || k % 256) return 0;

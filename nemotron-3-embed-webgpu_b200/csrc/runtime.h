@@ -24,8 +24,7 @@ struct Segment {
   int fmt = 0;        // SegFormat
   int row0 = 0;
   int rows = 0;
-  uint8_t* raw = nullptr;  // device copy of the pack bytes
-  size_t bytes = 0;
+  size_t bytes = 0;  // the pack's block bytes (decoded at load, not kept on the device)
 };
 
 struct Projection {

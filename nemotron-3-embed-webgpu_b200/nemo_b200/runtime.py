@@ -54,6 +54,7 @@ def load_library() -> ctypes.CDLL:
     sig = {
         "nemo_model_load": (I, [P, S, P, I, ctypes.POINTER(P)]),
         "nemo_model_destroy": (None, [P]),
+        "nemo_pack_b200": (I, [P, S, P, S, ctypes.POINTER(S)]),
         "nemo_model_info_get": (I, [P, ctypes.POINTER(ModelInfo)]),
         "nemo_plan_create": (I, [P, U32, U32, ctypes.POINTER(P)]),
         "nemo_plan_create_ex": (I, [P, U32, U32, U32, ctypes.POINTER(P)]),
@@ -105,6 +106,18 @@ def check(rc: int) -> None:
 
 def _ptr(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def pack_b200(wgpack: bytes) -> bytes:
+    """A B200-tiled copy of a .wgpack (nemo_pack_b200; host only): projections
+    stored as the tile-slab images the kernels stream, loaded without re-tiling."""
+    src = np.frombuffer(wgpack, dtype=np.uint8)
+    need = ctypes.c_size_t()
+    L = load_library()
+    check(L.nemo_pack_b200(_ptr(src), src.size, None, 0, ctypes.byref(need)))
+    out = np.empty(need.value, np.uint8)
+    check(L.nemo_pack_b200(_ptr(src), src.size, _ptr(out), out.size, ctypes.byref(need)))
+    return out.tobytes()
 
 
 def merged_length(sequence: int) -> int:

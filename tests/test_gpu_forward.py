@@ -303,3 +303,27 @@ def test_exact_attention_long_request():
     finally:
         gpu.destroy()
         orc.close()
+
+
+@pytest.mark.parametrize("flavour", ["kquant", "q40"])
+def test_b200_tiled_pack_matches_source_pack(flavour):
+    """A pack rewritten by nemo_pack_b200 (projections stored as the tile-slab
+    images the kernels stream; the f16 weights decoded from them on the
+    device) gives bit-identical embeddings to the source pack, on the
+    single-launch (<= 16 tokens) and batched paths."""
+    from nemo_b200.runtime import pack_b200
+    with open(synth.cached_model_pack(2, flavour, 5), "rb") as f:
+        data = f.read()
+    src = NemotronB200Model(data)
+    b2 = NemotronB200Model(pack_b200(data))
+    try:
+        assert b2.info().packed_weight_bytes > 0
+        for lengths in ([15], [300, 170]):
+            reqs = synth.make_requests(12, lengths)
+            ids, lens, seq = synth.pad_batch(reqs)
+            a = src.create_plan(len(lengths), seq).run_array(ids, lens).copy()
+            b = b2.create_plan(len(lengths), seq).run_array(ids, lens).copy()
+            assert np.array_equal(a, b), lengths
+    finally:
+        src.destroy()
+        b2.destroy()
