@@ -241,12 +241,14 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
       for (int i = 0; i < kTile; ++i) s[i] = __uint_as_float(sr[i]);
       const int valid = min(kTile, nkeys - j * kTile);
+      // The max of the raw scores, scaled once (scale > 0 keeps the order).
       float tmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < kTile; ++i) {
-        s[i] = i < valid ? s[i] * scale : -INFINITY;
+        s[i] = i < valid ? s[i] : -INFINITY;
         tmax = fmaxf(tmax, s[i]);
       }
+      tmax *= scale;
       // The running max of the warp's rows moves only when some row's tile
       // max exceeds it by more than kMaxSlack (log2 units). Otherwise P is
       // taken against the stale max: P <= 2^kMaxSlack, well inside f16, and
@@ -254,12 +256,17 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       // (With the exact running max nearly every tile moves some row's max.)
       const bool move = __any_sync(0xffffffffu, tmax > m + kMaxSlack);  // always on the first tile
       const float mnew = move ? fmaxf(m, tmax) : m;
-      float rsum = 0.f;
+      // p = 2^(s * scale - mnew): one FMA per score on the raw value.
+      const float nm = -mnew;
+      float rs0 = 0.f, rs1 = 0.f;  // two independent sum chains
 #pragma unroll
-      for (int i = 0; i < kTile; ++i) {
-        s[i] = ex2(s[i] - mnew);
-        rsum += s[i];
+      for (int i = 0; i < kTile; i += 2) {
+        s[i] = ex2(fmaf(s[i], scale, nm));
+        s[i + 1] = ex2(fmaf(s[i + 1], scale, nm));
+        rs0 += s[i];
+        rs1 += s[i + 1];
       }
+      const float rsum = rs0 + rs1;
       const float alpha = ex2(m - mnew);  // 0 on the first tile, 1 while the max stays
       // P_t (f16) over its own S columns: S_t(j) has been read, and neither
       // PV_t(j) nor S_t(j + 1) is issued before p_ready
