@@ -152,6 +152,25 @@ int nemo_plan_run_debug(nemo_plan* plan, const uint32_t* ids, size_t n_ids, cons
 /* Frees the plan's buffers, graphs and streams. */
 void nemo_plan_destroy(nemo_plan* plan);
 
+/* Host tokenizer (no GPU): text -> token ids for nemo_plan_run, in place of
+ * the browser tokenizer the reference loads with
+ * AutoTokenizer.from_pretrained('nvidia/Nemotron-3-Embed-1B-BF16')
+ * (src/main.ts:164-165) and calls as tokenizer(text).input_ids
+ * (src/webgpu/embedding-engine.ts:41). nemo_tokenizer_load reads a Hugging
+ * Face tokenizer.json of the byte-level BPE family: added tokens, no
+ * normalizer, Split(regex) + ByteLevel or ByteLevel(use_regex) pre-tokenizer
+ * (the Tekken and GPT-2 patterns), BPE merges, and a TemplateProcessing,
+ * Bert/Roberta or ByteLevel post-processor; other components fail with
+ * NEMO_ERR_FORMAT naming them. nemo_tokenizer_encode writes the ids of a
+ * UTF-8 text (post-processor special tokens included) to ids (capacity
+ * entries; ids == NULL only sets *n_ids). A tokenizer is immutable after load
+ * and may be shared by threads. */
+typedef struct nemo_tokenizer nemo_tokenizer;
+int nemo_tokenizer_load(const void* tokenizer_json, size_t bytes, nemo_tokenizer** out);
+int nemo_tokenizer_encode(const nemo_tokenizer* tokenizer, const char* text, size_t len, uint32_t* ids,
+                          size_t capacity, size_t* n_ids);
+void nemo_tokenizer_destroy(nemo_tokenizer* tokenizer);
+
 /* contextualMergedLength (src/webgpu/model.ts:30-32). */
 uint32_t nemo_merged_length(uint32_t sequence);
 

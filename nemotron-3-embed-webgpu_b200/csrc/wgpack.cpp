@@ -1,4 +1,5 @@
 #include "wgpack.h"
+#include "json_reader.h"
 
 #include <string.h>
 
@@ -7,152 +8,8 @@
 namespace nemo {
 namespace {
 
-// Minimal JSON reader for the .wgpack header: objects, arrays, strings
-// (with escapes), numbers, true/false/null.
-struct Json {
-  enum Kind { kNull, kBool, kNum, kStr, kArr, kObj } kind = kNull;
-  bool b = false;
-  double num = 0;
-  std::string str;
-  std::vector<Json> arr;
-  std::vector<std::pair<std::string, Json>> obj;
-  const Json* get(const char* key) const {
-    for (const auto& kv : obj)
-      if (kv.first == key) return &kv.second;
-    return nullptr;
-  }
-};
-
-struct Reader {
-  const char* p;
-  const char* end;
-  std::string err;
-  int depth = 0;
-
-  void ws() {
-    while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
-  }
-  bool fail(const char* m) {
-    if (err.empty()) err = m;
-    return false;
-  }
-  bool parse_string(std::string* s) {
-    if (p >= end || *p != '"') return fail("expected string");
-    ++p;
-    while (p < end && *p != '"') {
-      char c = *p++;
-      if (c == '\\') {
-        if (p >= end) return fail("bad escape");
-        char e = *p++;
-        switch (e) {
-          case '"': s->push_back('"'); break;
-          case '\\': s->push_back('\\'); break;
-          case '/': s->push_back('/'); break;
-          case 'b': s->push_back('\b'); break;
-          case 'f': s->push_back('\f'); break;
-          case 'n': s->push_back('\n'); break;
-          case 'r': s->push_back('\r'); break;
-          case 't': s->push_back('\t'); break;
-          case 'u': {
-            if (end - p < 4) return fail("bad \\u escape");
-            unsigned cp = 0;
-            for (int i = 0; i < 4; ++i) {
-              char h = *p++;
-              cp <<= 4;
-              if (h >= '0' && h <= '9') cp |= h - '0';
-              else if (h >= 'a' && h <= 'f') cp |= h - 'a' + 10;
-              else if (h >= 'A' && h <= 'F') cp |= h - 'A' + 10;
-              else return fail("bad \\u escape");
-            }
-            // Encode the code unit as UTF-8 (surrogates are kept as-is).
-            if (cp < 0x80) s->push_back((char)cp);
-            else if (cp < 0x800) {
-              s->push_back((char)(0xC0 | (cp >> 6)));
-              s->push_back((char)(0x80 | (cp & 0x3F)));
-            } else {
-              s->push_back((char)(0xE0 | (cp >> 12)));
-              s->push_back((char)(0x80 | ((cp >> 6) & 0x3F)));
-              s->push_back((char)(0x80 | (cp & 0x3F)));
-            }
-            break;
-          }
-          default: return fail("bad escape");
-        }
-      } else {
-        s->push_back(c);
-      }
-    }
-    if (p >= end) return fail("unterminated string");
-    ++p;
-    return true;
-  }
-  bool parse(Json* v) {
-    if (++depth > 64) return fail("JSON nested too deeply");
-    ws();
-    if (p >= end) return fail("unexpected end of JSON");
-    bool ok = true;
-    if (*p == '{') {
-      ++p;
-      v->kind = Json::kObj;
-      ws();
-      if (p < end && *p == '}') {
-        ++p;
-      } else {
-        for (;;) {
-          ws();
-          std::string key;
-          if (!parse_string(&key)) { ok = false; break; }
-          ws();
-          if (p >= end || *p != ':') { ok = fail("expected ':'"); break; }
-          ++p;
-          Json child;
-          if (!parse(&child)) { ok = false; break; }
-          v->obj.emplace_back(std::move(key), std::move(child));
-          ws();
-          if (p < end && *p == ',') { ++p; continue; }
-          if (p < end && *p == '}') { ++p; break; }
-          ok = fail("expected ',' or '}'");
-          break;
-        }
-      }
-    } else if (*p == '[') {
-      ++p;
-      v->kind = Json::kArr;
-      ws();
-      if (p < end && *p == ']') {
-        ++p;
-      } else {
-        for (;;) {
-          Json child;
-          if (!parse(&child)) { ok = false; break; }
-          v->arr.push_back(std::move(child));
-          ws();
-          if (p < end && *p == ',') { ++p; continue; }
-          if (p < end && *p == ']') { ++p; break; }
-          ok = fail("expected ',' or ']'");
-          break;
-        }
-      }
-    } else if (*p == '"') {
-      v->kind = Json::kStr;
-      ok = parse_string(&v->str);
-    } else if (end - p >= 4 && !strncmp(p, "true", 4)) {
-      v->kind = Json::kBool; v->b = true; p += 4;
-    } else if (end - p >= 5 && !strncmp(p, "false", 5)) {
-      v->kind = Json::kBool; v->b = false; p += 5;
-    } else if (end - p >= 4 && !strncmp(p, "null", 4)) {
-      v->kind = Json::kNull; p += 4;
-    } else {
-      const char* s = p;
-      while (p < end && (strchr("+-0123456789.eE", *p) != nullptr)) ++p;
-      if (p == s) return fail("unexpected character in JSON");
-      v->kind = Json::kNum;
-      v->num = strtod(std::string(s, p).c_str(), nullptr);
-    }
-    --depth;
-    return ok;
-  }
-};
+using json::Json;
+using json::Reader;
 
 bool num_is(const Json* v, double x) { return v && v->kind == Json::kNum && v->num == x; }
 

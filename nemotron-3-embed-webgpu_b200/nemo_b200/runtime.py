@@ -90,6 +90,9 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_qmatmul_enqueue": (I, [I, P, P, I, I, I, P, P, P]),
         "nemo_op_qmatmul": (I, [I, P, P, I, I, I, P]),
         "nemo_hp_pack_columns": (I, [I, P]),
+        "nemo_tokenizer_load": (I, [P, S, ctypes.POINTER(P)]),
+        "nemo_tokenizer_encode": (I, [P, P, S, P, S, ctypes.POINTER(S)]),
+        "nemo_tokenizer_destroy": (None, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -118,6 +121,45 @@ def pack_b200(wgpack: bytes) -> bytes:
     out = np.empty(need.value, np.uint8)
     check(L.nemo_pack_b200(_ptr(src), src.size, _ptr(out), out.size, ctypes.byref(need)))
     return out.tobytes()
+
+
+class NemotronTokenizer:
+    """The host tokenizer (nemo_tokenizer_*) over a Hugging Face tokenizer.json.
+    Called like the browser tokenizer the reference's engine uses
+    (src/webgpu/embedding-engine.ts:41): tokenizer(text)["input_ids"] is a
+    [1 x n] array whose first id is the post-processor's BOS."""
+
+    def __init__(self, tokenizer_json: bytes | str):
+        if isinstance(tokenizer_json, str):
+            with open(tokenizer_json, "rb") as f:
+                tokenizer_json = f.read()
+        buf = np.frombuffer(tokenizer_json, dtype=np.uint8)
+        h = ctypes.c_void_p()
+        check(load_library().nemo_tokenizer_load(_ptr(buf), buf.size, ctypes.byref(h)))
+        self._h = h
+
+    def encode(self, text: str) -> list[int]:
+        raw = text.encode("utf-8")
+        n = ctypes.c_size_t()
+        L = load_library()
+        check(L.nemo_tokenizer_encode(self._h, raw, len(raw), None, 0, ctypes.byref(n)))
+        ids = np.empty(max(n.value, 1), np.uint32)
+        check(L.nemo_tokenizer_encode(self._h, raw, len(raw), _ptr(ids), ids.size, ctypes.byref(n)))
+        return ids[:n.value].tolist()
+
+    def __call__(self, text: str) -> dict:
+        return {"input_ids": np.array([self.encode(text)], dtype=np.int64)}
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            load_library().nemo_tokenizer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def merged_length(sequence: int) -> int:
