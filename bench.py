@@ -571,7 +571,11 @@ def head_parallel_workload(ndist, rinfo, pack: str, args, single_req_s) -> dict 
     ndist.cpu_barrier(rinfo)
     entry = None
     if rank == 0:
-        model = NemotronB200Model(pack, devices=list(range(world)))
+        try:
+            model = NemotronB200Model(pack, devices=list(range(world)))
+        except Exception as e:  # recorded, and every rank still takes the barrier below
+            model, entry = None, {"error": f"{type(e).__name__}: {e}", "n_devices": world}
+    if rank == 0 and model is not None:
         try:
             reqs = synth.make_requests(args.seed, [5000])
             ids, lens, seq = synth.pad_batch(reqs)
@@ -593,6 +597,8 @@ def head_parallel_workload(ndist, rinfo, pack: str, args, single_req_s) -> dict 
                      "speedup_vs_single_device": (value / single_req_s) if single_req_s else None,
                      "e2e": {"value": value, "unit": "req/s", "h2d_bytes_per_step": ids.nbytes + 4,
                              "d2h_bytes_per_step": out.nbytes}}
+        except Exception as e:  # a failed run (bounded by the plan's host deadline) is recorded
+            entry = {"error": f"{type(e).__name__}: {e}", "n_devices": world}
         finally:
             model.destroy()
     ndist.cpu_barrier(rinfo)

@@ -34,23 +34,24 @@ def test_two_device_plan_matches_single_device():
         assert cos >= 0.9999, (i, cos)
 
 
+@pytest.mark.parametrize("n_dev", [2, 4, 8])
 @pytest.mark.parametrize("length", [700, 2300])
-def test_head_parallel_matches_single_device(length, monkeypatch):
-    """One long request on a two-device plan runs head-parallel (token-sharded
+def test_head_parallel_matches_single_device(length, n_dev, monkeypatch):
+    """One long request on a 2-, 4- or 8-device plan runs head-parallel (token-sharded
     projections, NCCL all-to-all around attention, all-gathers for the merge
     and the pool); 2300 tokens also samples every third key before the merge.
     The embedding must match the single-device run, and the eager first run,
     the captured second run and the replayed third run must agree bit for bit."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < n_dev:
+        pytest.skip(f"needs {n_dev} GPUs")
     path = synth.cached_model_pack(3, "kquant", 5)
     with open(path, "rb") as f:
         data = f.read()
     reqs = synth.make_requests(9, [length], vocab=synth.VOCAB)
     ids, lens, seq = synth.pad_batch(reqs)
     one = NemotronB200Model(data, devices=[0])
-    two = NemotronB200Model(data, devices=[0, 1])
+    two = NemotronB200Model(data, devices=list(range(n_dev)))
     try:
         monkeypatch.setenv("NEMO_HEAD_PARALLEL_MIN", "512")
         plan2 = two.create_plan(1, seq)
