@@ -562,7 +562,8 @@ def qmatmul_workload(torch, ndist, rinfo, args) -> dict:
 
 def head_parallel_workload(ndist, rinfo, pack: str, args, single_req_s) -> dict | None:
     """config5hp: one 5000-token request head-parallel over all N GPUs of the
-    box (token-sharded projections, NCCL all-to-all around attention), from
+    box (token-sharded projections; the QKV and attention epilogues store into
+    the devices owning each head group / token row over NVLink peer memory), from
     rank 0's process through nemo_plan_run with host buffers. The other ranks
     wait on a host-only barrier meanwhile. Every rank takes the same barriers."""
     from nemo_b200 import synth

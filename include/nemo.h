@@ -124,8 +124,9 @@ int nemo_plan_single_launch(nemo_plan* plan);
 
 /* For a plan of batch 1 on 2, 4 or 8 devices: the request length from which
  * nemo_plan_run runs the request head-parallel across the devices (token-
- * sharded projections, NCCL all-to-all around attention); 0 when the plan has
- * no head-parallel path. Default 5000 tokens, NEMO_HEAD_PARALLEL_MIN at plan
+ * sharded projections; the QKV and attention epilogues store into the devices
+ * owning each head group / token row over peer memory); 0 when the plan has
+ * no head-parallel path (also when the devices lack peer access). Default 5000 tokens, NEMO_HEAD_PARALLEL_MIN at plan
  * creation overrides. Build-specific introspection; no reference counterpart. */
 int nemo_plan_head_parallel(nemo_plan* plan);
 

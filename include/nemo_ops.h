@@ -120,11 +120,15 @@ int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m
                             void* d_err, void* stream);
 int nemo_op_qmatmul(int fmt, const void* d_packed, const void* d_x, int m, int n, int k, void* d_y);
 
-/* Column map of the head-parallel exchange (no reference counterpart; the
- * index function hp_pack_kernel uses, exported for layout tests without a
- * GPU): for n_devices in {2, 4, 8}, columns[c] (c < 5120) is the QKV column
- * that column c of the concatenated per-device send blocks carries. */
-int nemo_hp_pack_columns(int n_devices, int* columns);
+/* Routing of the head-parallel path (no reference counterpart; the index
+ * functions its QKV GEMM and attention epilogues use, exported for layout
+ * tests without a GPU), n_devices in {2, 4, 8}:
+ * nemo_hp_qkv_route: for each QKV column c < 5120, the device that owns its
+ *   head group, the buffer there (0 Q, 1 K, 2 V) and the column in it;
+ * nemo_hp_row_owner: for positions 0..n_positions-1 of a request sharded in
+ *   rows_per_device-row shards (the last one shorter), the owning device. */
+int nemo_hp_qkv_route(int n_devices, int* device, int* buffer, int* column);
+int nemo_hp_row_owner(int n_devices, int rows_per_device, int n_positions, int* device);
 
 #ifdef __cplusplus
 }

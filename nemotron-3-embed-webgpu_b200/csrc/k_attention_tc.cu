@@ -58,6 +58,7 @@ struct AttnTcArgs {
   uint32_t* err;
   int v_col0;  // column of the head group's V in the rows of the v map
   int out_ld;  // output row stride (q heads of the group x 128)
+  AttnScatter scatter;  // scatter.dst[0] set: rows go to the devices that own them
 };
 
 __global__ void __launch_bounds__(kThreadsA, 1)
@@ -306,7 +307,19 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done + 8 * t, (ntiles - 1) & 1, a.err))) {
       dev::tc_fence_after();
       const float inv = 1.0f / l;
-      __half* dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
+      // Head-parallel runs store each output row straight into the attention
+      // buffer of the device that owns the row's token shard (peer memory over
+      // NVLink), at this head group's columns.
+      __half* dst;
+      if (a.scatter.dst[0]) {
+        const int owner = hp_row_owner(pos, a.scatter.rows_per_dev, a.scatter.n_dev);
+        __half* buf = a.scatter.dst[0];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) buf = owner == i ? a.scatter.dst[i] : buf;  // selects, no local copy
+        dst = buf + (size_t)(pos - owner * a.scatter.rows_per_dev) * kQWidth + a.scatter.col0 + h * kHeadDim;
+      } else {
+        dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
@@ -375,14 +388,17 @@ cudaError_t launch_gather_sampled_group(const __half* k, const __half* qkv, int 
 cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
                                 __half* out, uint32_t* err, cudaStream_t s) {
   return launch_attention_tc_group(maps, meta, merged, batch, max_len, kQHeads, kQWidth + kKVWidth, kQWidth, out, err,
-                                   s);
+                                   s, nullptr);
 }
 
 cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
                                       int q_heads, int v_col0, int out_ld, __half* out, uint32_t* err,
-                                      cudaStream_t s) {
+                                      cudaStream_t s, const AttnScatter* scatter) {
   if (max_len <= 0 || batch <= 0) return cudaSuccess;
   if (q_heads <= 0 || q_heads % (kQHeads / kKVHeads) || v_col0 % 8 || out_ld % 8) return cudaErrorInvalidValue;
+  if (scatter && (batch != 1 || scatter->n_dev < 1 || scatter->n_dev > 8 || scatter->rows_per_dev < 1 ||
+                  scatter->col0 % 8 || !scatter->dst[0]))
+    return cudaErrorInvalidValue;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -393,7 +409,8 @@ cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bo
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  AttnTcArgs a{meta, merged ? 1 : 0, out, err, v_col0, out_ld};
+  AttnTcArgs a{meta, merged ? 1 : 0, out, err, v_col0, out_ld, {}};
+  if (scatter) a.scatter = *scatter;
   dim3 grid((max_len + 2 * kTile - 1) / (2 * kTile), q_heads, batch);
   attention_tc_kernel<<<grid, kThreadsA, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
   return cudaGetLastError();

@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(192, 1)
           const int* off = e.merged ? e.meta->tgt_off : e.meta->src_off;
           int b = 0;
           while (b + 1 < e.meta->batch && row >= off[b + 1]) ++b;
-          pos = row - off[b];
+          pos = row - off[b] + e.hp.row0;  // row0: shard offset of a head-parallel run, else 0
         }
         // The 32 table floats (16 cos/sin pairs, 128 contiguous bytes) of a
         // chunk's rotated columns are loaded one chunk ahead, so their latency
@@ -235,26 +235,58 @@ __global__ void __launch_bounds__(192, 1)
           load_cs(c + 1, cs_nxt);
           dev::tc_wait_ld();
           // no early exit: every lane reaches the next (warp-collective) tcgen05.ld
-          if (row < M && e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
-            // (even, odd) column pairs rotated by the table row of pos, as the
-            // f16-stored QKV would be (k_misc.cu rope_kernel)
-            const float* tcs = reinterpret_cast<const float*>(cs_cur);
+          if (row < M && e.mode == kSkinnyRope && (col0 < kQWidth + kKVWidth || e.hp.n_dev)) {
             uint32_t o[16];
+            if (col0 < kQWidth + kKVWidth) {
+              // (even, odd) column pairs rotated by the table row of pos, as
+              // the f16-stored QKV would be (k_misc.cu rope_kernel)
+              const float* tcs = reinterpret_cast<const float*>(cs_cur);
 #pragma unroll
-            for (int p = 0; p < 16; ++p) {
-              const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
-              const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
-              const float2 tc = make_float2(tcs[2 * p], tcs[2 * p + 1]);
-              const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
-              const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
-              __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
-              o[p] = *reinterpret_cast<uint32_t*>(&h);
+              for (int p = 0; p < 16; ++p) {
+                const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
+                const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
+                const float2 tc = make_float2(tcs[2 * p], tcs[2 * p + 1]);
+                const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
+                const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
+                __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
+                o[p] = *reinterpret_cast<uint32_t*>(&h);
+              }
+            } else {
+#pragma unroll
+              for (int p = 0; p < 16; ++p) {
+                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
+                o[p] = *reinterpret_cast<uint32_t*>(&h);
+              }
             }
-            __half* dst = col0 < kQWidth ? e.q + (size_t)row * kQWidth + col0
-                                         : e.k + (size_t)row * kKVWidth + (col0 - kQWidth);
+            if (e.hp.n_dev) {
+              // the owning device's Q / K / V row (and compact row when sampled)
+              int j, b, dc;
+              hp_qkv_route(col0, e.hp.n_dev, &j, &b, &dc);
+              const int w = b == 0 ? kQWidth / e.hp.n_dev : kKVWidth / e.hp.n_dev;
+              __half *dst = nullptr, *cdst = nullptr;
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              for (int i = 0; i < 8; ++i)  // selects, no local copy of the pointer arrays
+                if (i == j) {
+                  dst = b == 0 ? e.hp.q[i] : b == 1 ? e.hp.k[i] : e.hp.v[i];
+                  cdst = b == 1 ? e.hp.kc[i] : e.hp.vc[i];
+                }
+              dst += (size_t)pos * w + dc;
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              if (e.hp.sample && b > 0 && pos % kSampleStride == 0) {
+                cdst += (size_t)(pos / kSampleStride) * w + dc;
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                  reinterpret_cast<uint4*>(cdst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              }
+            } else {
+              __half* dst = col0 < kQWidth ? e.q + (size_t)row * kQWidth + col0
+                                           : e.k + (size_t)row * kKVWidth + (col0 - kQWidth);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
           } else if (row < M && splits > 1) {
             // f32 partial sums of split sp (summed by the consumer in split order)
             float4* dst = reinterpret_cast<float4*>(e.part + ((size_t)sp * M + row) * (n_tiles * BN) + col0);
@@ -334,7 +366,15 @@ cudaError_t launch_gemm_tc_epi(const CUtensorMap* ma, const CUtensorMap* mb, __h
                                int max_rows, int n, int k, int bn, const GemmEpi& ep, uint32_t* err, cudaStream_t s) {
   if (k % 64 != 0 || n % bn != 0) return cudaErrorInvalidValue;
   if (ep.mode == kSkinnySwiglu && (bn < 128 || n != 2 * kInter)) return cudaErrorInvalidValue;
-  if (ep.mode == kSkinnyRope && (n != kQKVWidth || !ep.meta || !ep.rope || !ep.q || !ep.k)) return cudaErrorInvalidValue;
+  if (ep.mode == kSkinnyRope && (n != kQKVWidth || !ep.meta || !ep.rope || (!ep.hp.n_dev && (!ep.q || !ep.k))))
+    return cudaErrorInvalidValue;
+  if (ep.hp.n_dev) {
+    const int nd = ep.hp.n_dev;
+    if (ep.mode != kSkinnyRope || (nd != 2 && nd != 4 && nd != 8) || ep.hp.row0 < 0) return cudaErrorInvalidValue;
+    for (int i = 0; i < nd; ++i)
+      if (!ep.hp.q[i] || !ep.hp.k[i] || !ep.hp.v[i] || (ep.hp.sample && (!ep.hp.kc[i] || !ep.hp.vc[i])))
+        return cudaErrorInvalidValue;
+  }
   if ((ep.part != nullptr) != (ep.splits_out != nullptr) || (ep.part && ep.mode != kSkinnyPlain))
     return cudaErrorInvalidValue;
   switch (bn) {

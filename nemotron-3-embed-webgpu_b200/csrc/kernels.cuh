@@ -81,10 +81,44 @@ cudaError_t launch_attention_tc(const AttnMaps& maps, const Meta* meta, bool mer
 cudaError_t launch_gather_sampled(const __half* k, const __half* qkv, const Meta* meta, bool merged, int max_rows,
                                   __half* kc, __half* vc, cudaStream_t s);
 // Head-group variants (head-parallel attention): q_heads q heads with their
-// q_heads/3 kv heads; V at column v_col0 of the v map's rows; out rows out_ld wide.
+// q_heads/3 kv heads; V at column v_col0 of the v map's rows; out rows out_ld
+// wide, or, with scatter (batch 1), row p stored at
+// dst[p / rows_per_dev] + (p % rows_per_dev) * 3072 + col0 + head * 128: the
+// attention buffer of the device owning the row (peer memory).
+// Head-parallel routing over n devices (2, 4 or 8). Device j owns head group
+// j: q heads j*24/n.. (QKV columns [j*3072/n, (j+1)*3072/n)) and kv heads
+// j*8/n.. (K and V columns [j*1024/n, (j+1)*1024/n) after their offsets), so
+// each GQA group of 3 q heads stays with its kv head. QKV column c goes to
+// buffer *buf (0 Q, 1 K, 2 V) of device *dev at column *dcol (Q rows 3072/n
+// wide, K and V rows 1024/n wide).
+__host__ __device__ inline void hp_qkv_route(int c, int n, int* dev, int* buf, int* dcol) {
+  const int gq = kQWidth / n, gk = kKVWidth / n;
+  if (c < kQWidth) {
+    *dev = c / gq, *buf = 0, *dcol = c - *dev * gq;
+  } else if (c < kQWidth + kKVWidth) {
+    c -= kQWidth;
+    *dev = c / gk, *buf = 1, *dcol = c - *dev * gk;
+  } else {
+    c -= kQWidth + kKVWidth;
+    *dev = c / gk, *buf = 2, *dcol = c - *dev * gk;
+  }
+}
+// Token position pos of a request sharded in rows_per_dev-row shards (the last
+// one shorter) belongs to this device.
+__host__ __device__ inline int hp_row_owner(int pos, int rows_per_dev, int n) {
+  const int o = pos / rows_per_dev;
+  return o < n - 1 ? o : n - 1;
+}
+
+struct AttnScatter {
+  __half* dst[8];
+  int n_dev;
+  int rows_per_dev;
+  int col0;
+};
 cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bool merged, int batch, int max_len,
                                       int q_heads, int v_col0, int out_ld, __half* out, uint32_t* err,
-                                      cudaStream_t s);
+                                      cudaStream_t s, const AttnScatter* scatter = nullptr);
 cudaError_t launch_gather_sampled_group(const __half* k, const __half* qkv, int qkv_ld, int v_col0, int kv_w,
                                         const Meta* meta, bool merged, int max_rows, __half* kc, __half* vc,
                                         cudaStream_t s);
@@ -130,6 +164,22 @@ struct GemmEpi {
   // The split count used is stored at *splits_out (set with part).
   float* part = nullptr;
   int* splits_out = nullptr;
+  // Head-parallel QKV (RoPE mode, hp.n_dev > 0): local row r is token position
+  // hp.row0 + r of one request; each 32-column chunk is stored, Q and K
+  // rotated, at that row of the Q, K or V buffer of the device owning its head
+  // group (hp_qkv_route): peer memory over NVLink. With hp.sample set the K
+  // and V of every third position also go to row pos / 3 of that device's
+  // compact kc / vc buffers (the keys attention samples above 2048).
+  struct {
+    __half* q[8] = {};
+    __half* k[8] = {};
+    __half* v[8] = {};
+    __half* kc[8] = {};
+    __half* vc[8] = {};
+    int n_dev = 0;
+    int row0 = 0;
+    int sample = 0;
+  } hp;
 };
 
 // K splits of the persistent GEMM for m_tiles x n_tiles output tiles of kt

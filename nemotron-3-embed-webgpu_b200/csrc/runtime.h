@@ -158,7 +158,7 @@ struct nemo_plan {
   int batch = 0, seq = 0;
   std::vector<std::unique_ptr<nemo::DevicePlan>> devs;
   // Multi-device plans of batch 1: requests of at least hp_min tokens run
-  // head-parallel over all devices (NCCL); shorter ones run on one device.
+  // head-parallel over all devices (peer memory); shorter ones run on one device.
   nemo::HeadPar* hp = nullptr;
   int hp_min = 0;
   bool exact = false;  // NEMO_PLAN_EXACT_ATTENTION

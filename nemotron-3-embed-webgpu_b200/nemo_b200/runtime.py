@@ -89,7 +89,8 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_qmatmul_image": (I, [I, P, I, I, P]),
         "nemo_op_qmatmul_enqueue": (I, [I, P, P, I, I, I, P, P, P]),
         "nemo_op_qmatmul": (I, [I, P, P, I, I, I, P]),
-        "nemo_hp_pack_columns": (I, [I, P]),
+        "nemo_hp_qkv_route": (I, [I, P, P, P]),
+        "nemo_hp_row_owner": (I, [I, I, I, P]),
         "nemo_tokenizer_load": (I, [P, S, ctypes.POINTER(P)]),
         "nemo_tokenizer_encode": (I, [P, P, S, P, S, ctypes.POINTER(S)]),
         "nemo_tokenizer_destroy": (None, [P]),

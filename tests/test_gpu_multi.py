@@ -38,10 +38,13 @@ def test_two_device_plan_matches_single_device():
 @pytest.mark.parametrize("length", [700, 2300])
 def test_head_parallel_matches_single_device(length, n_dev, monkeypatch):
     """One long request on a 2-, 4- or 8-device plan runs head-parallel (token-sharded
-    projections, NCCL all-to-all around attention, all-gathers for the merge
-    and the pool); 2300 tokens also samples every third key before the merge.
-    The embedding must match the single-device run, and the eager first run,
-    the captured second run and the replayed third run must agree bit for bit."""
+    projections; the QKV GEMM epilogue stores Q/K/V into the devices owning each
+    head group and the attention epilogue stores rows into the devices owning
+    them, over peer memory; peer copies gather rows for the merge and the
+    pool); 2300 tokens also samples every third key before the merge. The
+    embedding must match the single-device run, and the directly issued first
+    run, the captured second run and the replayed third run must agree bit for
+    bit."""
     import torch
     if torch.cuda.device_count() < n_dev:
         pytest.skip(f"needs {n_dev} GPUs")
@@ -56,8 +59,8 @@ def test_head_parallel_matches_single_device(length, n_dev, monkeypatch):
         monkeypatch.setenv("NEMO_HEAD_PARALLEL_MIN", "512")
         plan2 = two.create_plan(1, seq)
         assert plan2.head_parallel_min == 512
-        b = plan2.run_array(ids, lens).copy()   # eager (sets up the NCCL peer connections)
-        b2 = plan2.run_array(ids, lens).copy()  # captured as one CUDA graph per device, then launched
+        b = plan2.run_array(ids, lens).copy()   # issued directly
+        b2 = plan2.run_array(ids, lens).copy()  # captured as one multi-device CUDA graph, then launched
         b3 = plan2.run_array(ids, lens).copy()  # graph replay
         plan1 = one.create_plan(1, seq)
         assert plan1.head_parallel_min == 0
