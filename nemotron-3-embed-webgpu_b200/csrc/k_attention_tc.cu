@@ -307,32 +307,56 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     if (ok && __all_sync(0xffffffffu, dev::mbar_wait(pv_done + 8 * t, (ntiles - 1) & 1, a.err))) {
       dev::tc_fence_after();
       const float inv = 1.0f / l;
-      // Head-parallel runs store each output row straight into the attention
-      // buffer of the device that owns the row's token shard (peer memory over
-      // NVLink), at this head group's columns.
-      __half* dst;
+      auto out_unit = [&](const uint32_t (&r)[32], int v) {
+        return make_uint4(pack_h2f(__uint_as_float(r[v * 8]) * inv, __uint_as_float(r[v * 8 + 1]) * inv),
+                          pack_h2f(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv),
+                          pack_h2f(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv),
+                          pack_h2f(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv));
+      };
       if (a.scatter.dst[0]) {
-        const int owner = hp_row_owner(pos, a.scatter.rows_per_dev, a.scatter.n_dev);
-        __half* buf = a.scatter.dst[0];
+        // Head-parallel: each output row goes to the attention buffer of the
+        // device owning the row's token shard (peer memory over NVLink), at
+        // this head group's columns. The warp stages its 32 rows x 128
+        // columns in its quarter of the Q_t tile (every MMA reading Q_t has
+        // retired) and writes each row as one 256-byte segment, 16 lanes per
+        // row; 16-byte unit u of row i sits at unit u ^ (i & 7).
+        uint8_t* stage = sQ + t * kTileBytes + quarter * (32 * 256);
 #pragma unroll
-        for (int i = 1; i < 8; ++i) buf = owner == i ? a.scatter.dst[i] : buf;  // selects, no local copy
-        dst = buf + (size_t)(pos - owner * a.scatter.rows_per_dev) * kQWidth + a.scatter.col0 + h * kHeadDim;
-      } else {
-        dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
-        dev::tc_wait_ld();
-        if (pos < len) {
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
+          dev::tc_wait_ld();
 #pragma unroll
           for (int v = 0; v < 4; ++v)
-            reinterpret_cast<uint4*>(dst + c * 32)[v] =
-                make_uint4(pack_h2f(__uint_as_float(r[v * 8]) * inv, __uint_as_float(r[v * 8 + 1]) * inv),
-                           pack_h2f(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv),
-                           pack_h2f(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv),
-                           pack_h2f(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv));
+            *reinterpret_cast<uint4*>(stage + lane * 256 + (((c * 4 + v) ^ (lane & 7)) * 16)) = out_unit(r, v);
+        }
+        __syncwarp();
+        const int u = lane & 15;
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int rr = it * 2 + (lane >> 4);
+          const int p = q0 + t * kTile + quarter * 32 + rr;
+          if (p < len) {
+            const int owner = hp_row_owner(p, a.scatter.rows_per_dev, a.scatter.n_dev);
+            __half* buf = a.scatter.dst[0];
+#pragma unroll
+            for (int i = 1; i < 8; ++i) buf = owner == i ? a.scatter.dst[i] : buf;  // selects, no local copy
+            *reinterpret_cast<uint4*>(buf + (size_t)(p - owner * a.scatter.rows_per_dev) * kQWidth +
+                                      a.scatter.col0 + h * kHeadDim + u * 8) =
+                *reinterpret_cast<const uint4*>(stage + rr * 256 + ((u ^ (rr & 7)) * 16));
+          }
+        }
+      } else {
+        __half* dst = a.out + (size_t)(base + pos) * a.out_ld + h * kHeadDim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          dev::tmem_ld_32x32b_x32(lane_base + colO + c * 32, r);
+          dev::tc_wait_ld();
+          if (pos < len) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst + c * 32)[v] = out_unit(r, v);
+          }
         }
       }
     }

@@ -38,8 +38,34 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i || MMAs of tile i + 1
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int STAGE_OUT = 4 * 32 * 128;  // per epilogue warp: 32 rows x 64 f16 (head-parallel stores)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + STAGE_OUT;
 };
+
+// (even, odd) column pairs of a 32-column accumulator chunk rounded to f16,
+// rotated by the 16 (cos, sin) table pairs cs, rounded again (as the
+// f16-stored QKV would be, k_misc.cu rope_kernel), packed as 16 half2.
+__device__ __forceinline__ void rope_pack(const uint32_t (&r)[32], const float4 (&cs)[8], uint32_t (&o)[16]) {
+  const float* tcs = reinterpret_cast<const float*>(cs);
+#pragma unroll
+  for (int p = 0; p < 16; ++p) {
+    const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
+    const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
+    const float2 tc = make_float2(tcs[2 * p], tcs[2 * p + 1]);
+    const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
+    const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
+    __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
+    o[p] = *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ void plain_pack(const uint32_t (&r)[32], uint32_t (&o)[16]) {
+#pragma unroll
+  for (int p = 0; p < 16; ++p) {
+    __half2 h = __floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
+    o[p] = *reinterpret_cast<uint32_t*>(&h);
+  }
+}
 
 // Persistent: CTA c takes tiles c, c + grid, ... of the (m tile, n tile)
 // grid in n-fastest order; M (valid token rows) is read on the device.
@@ -167,6 +193,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::mbar_wait(fin, 0, err, 100000000ull);
   } else {
     const int quarter = warp & 3;
+    uint8_t* stage = smem + C::STAGES * C::STAGE_BYTES + 256 + quarter * (32 * 128);
     int i = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
       const int buf = i & 1;
@@ -235,33 +262,30 @@ __global__ void __launch_bounds__(192, 1)
           load_cs(c + 1, cs_nxt);
           dev::tc_wait_ld();
           // no early exit: every lane reaches the next (warp-collective) tcgen05.ld
-          if (row < M && e.mode == kSkinnyRope && (col0 < kQWidth + kKVWidth || e.hp.n_dev)) {
+          if (e.hp.n_dev) {
+            // Head-parallel QKV (warp-uniform branch): the 32 x 32 chunk goes
+            // through this warp's shared-memory stage; every second chunk the
+            // warp writes the staged 32 rows x 64 columns out as 128-byte row
+            // segments (8 lanes per row), so each peer store is a whole line.
             uint32_t o[16];
-            if (col0 < kQWidth + kKVWidth) {
-              // (even, odd) column pairs rotated by the table row of pos, as
-              // the f16-stored QKV would be (k_misc.cu rope_kernel)
-              const float* tcs = reinterpret_cast<const float*>(cs_cur);
-#pragma unroll
-              for (int p = 0; p < 16; ++p) {
-                const float even = __half2float(__float2half_rn(__uint_as_float(r[2 * p])));
-                const float odd = __half2float(__float2half_rn(__uint_as_float(r[2 * p + 1])));
-                const float2 tc = make_float2(tcs[2 * p], tcs[2 * p + 1]);
-                const float first = __fsub_rn(__fmul_rn(even, tc.x), __fmul_rn(odd, tc.y));
-                const float second = __fadd_rn(__fmul_rn(even, tc.y), __fmul_rn(odd, tc.x));
-                __half2 h = __halves2half2(__float2half_rn(first), __float2half_rn(second));
-                o[p] = *reinterpret_cast<uint32_t*>(&h);
-              }
+            if (row < M) {
+              if (col0 < kQWidth + kKVWidth)
+                rope_pack(r, cs_cur, o);
+              else
+                plain_pack(r, o);
             } else {
 #pragma unroll
-              for (int p = 0; p < 16; ++p) {
-                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
-                o[p] = *reinterpret_cast<uint32_t*>(&h);
-              }
+              for (int p = 0; p < 16; ++p) o[p] = 0u;
             }
-            if (e.hp.n_dev) {
-              // the owning device's Q / K / V row (and compact row when sampled)
+            // 16-byte unit u of row `lane` at unit u ^ (lane & 7): conflict-free both ways
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((((c & 1) * 4 + v) ^ (lane & 7)) * 16)) =
+                  make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            if (c & 1) {
+              __syncwarp();
               int j, b, dc;
-              hp_qkv_route(col0, e.hp.n_dev, &j, &b, &dc);
+              hp_qkv_route(col0 - 32, e.hp.n_dev, &j, &b, &dc);  // 64 columns within one head
               const int w = b == 0 ? kQWidth / e.hp.n_dev : kKVWidth / e.hp.n_dev;
               __half *dst = nullptr, *cdst = nullptr;
 #pragma unroll
@@ -270,23 +294,30 @@ __global__ void __launch_bounds__(192, 1)
                   dst = b == 0 ? e.hp.q[i] : b == 1 ? e.hp.k[i] : e.hp.v[i];
                   cdst = b == 1 ? e.hp.kc[i] : e.hp.vc[i];
                 }
-              dst += (size_t)pos * w + dc;
+              const int u = lane & 7;
 #pragma unroll
-              for (int v = 0; v < 4; ++v)
-                reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-              if (e.hp.sample && b > 0 && pos % kSampleStride == 0) {
-                cdst += (size_t)(pos / kSampleStride) * w + dc;
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
-                  reinterpret_cast<uint4*>(cdst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              for (int it = 0; it < 8; ++it) {
+                const int rr = it * 4 + (lane >> 3);
+                const int lrow = m0 + quarter * 32 + rr;
+                if (lrow < M) {
+                  // one request starting at local row 0: position = row0 + local row
+                  const int p = e.hp.row0 + lrow;
+                  const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((u ^ (rr & 7)) * 16));
+                  *reinterpret_cast<uint4*>(dst + (size_t)p * w + dc + u * 8) = val;
+                  if (e.hp.sample && b > 0 && p % kSampleStride == 0)
+                    *reinterpret_cast<uint4*>(cdst + (size_t)(p / kSampleStride) * w + dc + u * 8) = val;
+                }
               }
-            } else {
-              __half* dst = col0 < kQWidth ? e.q + (size_t)row * kQWidth + col0
-                                           : e.k + (size_t)row * kKVWidth + (col0 - kQWidth);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              __syncwarp();
             }
+          } else if (row < M && e.mode == kSkinnyRope && col0 < kQWidth + kKVWidth) {
+            uint32_t o[16];
+            rope_pack(r, cs_cur, o);
+            __half* dst = col0 < kQWidth ? e.q + (size_t)row * kQWidth + col0
+                                         : e.k + (size_t)row * kKVWidth + (col0 - kQWidth);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
           } else if (row < M && splits > 1) {
             // f32 partial sums of split sp (summed by the consumer in split order)
             float4* dst = reinterpret_cast<float4*>(e.part + ((size_t)sp * M + row) * (n_tiles * BN) + col0);
