@@ -335,15 +335,25 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
           ok = false;
           break;
         }
-#pragma unroll 1
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q = grp + 2 * qq;
-          uint32_t h[32];
-          const RegSink sink{h};
-          if (fmt == kSegQ4K) decode_q4k(blk, q, sink);
-          else if (fmt == kSegQ6K) decode_q6k(blk, d6, q, sink);
-          else decode_q40(blk, q, sink);
-          dev::tmem_st_32x32b_x32(tm_a + lane_base + s * 128 + q * 32, h);
+        // Both quarters are decoded into separate registers before either
+        // TMEM store: the two independent chains fill the issue slots of the
+        // two decoder warps per scheduler (one quarter at a time, each store
+        // waiting on its source registers, ran at a third of that rate).
+        {
+          uint32_t ha[32], hb[32];
+          const RegSink sa{ha}, sb{hb};
+          if (fmt == kSegQ4K) {
+            decode_q4k(blk, grp, sa);
+            decode_q4k(blk, grp + 2, sb);
+          } else if (fmt == kSegQ6K) {
+            decode_q6k(blk, d6, grp, sa);
+            decode_q6k(blk, d6, grp + 2, sb);
+          } else {
+            decode_q40(blk, grp, sa);
+            decode_q40(blk, grp + 2, sb);
+          }
+          dev::tmem_st_32x32b_x32(tm_a + lane_base + s * 128 + grp * 32, ha);
+          dev::tmem_st_32x32b_x32(tm_a + lane_base + s * 128 + (grp + 2) * 32, hb);
         }
         dev::tc_wait_st();
         dev::tc_fence_before();
@@ -475,6 +485,45 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       return *reinterpret_cast<volatile int*>(&sh->flag) != 0;
     };
 
+    // A gate/up tile computed whole by this CTA: its accumulator goes from
+    // TMEM to shared memory (rows = 64 gate + 64 up columns) and the SwiGLU
+    // epilogue runs from there, with the arithmetic of the split-K epilogue
+    // above for a single slot.
+    auto drain_swiglu = [&](const FwdSeg& sg, int T) {
+      const int d = gseg & 1;
+      const bool got = __all_sync(0xffffffffu, wait(dfull + 8 * d, (gseg >> 1) & 1, err, lim));
+      ++gseg;
+      if (got) {
+        dev::tc_fence_after();
+        const int row = quarter * 32 + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < NP; c0 += 16) {
+          uint32_t v[16];
+          dev::tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + d * NP + c0, v);
+          dev::tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ebuf[(c0 + j) * 128 + row] = __uint_as_float(v[j]);
+        }
+      }
+      dev::tc_fence_before();
+      dev::mbar_arrive(dempty + 8 * d);
+      pw_sync();
+      if (got) {
+        const int r = pt & 63, tb = (pt >> 6) * (NP / 2);
+#pragma unroll
+        for (int j = 0; j < NP / 2; ++j) {
+          const int t = tb + j;
+          if (t >= T) break;
+          const float gh = __half2float(__float2half_rn(__fadd_rn(0.f, ebuf[t * 128 + r])));
+          const float uh = __half2float(__float2half_rn(__fadd_rn(0.f, ebuf[t * 128 + 64 + r])));
+          const float silu = __fdiv_rn(gh, __fadd_rn(1.0f, expf(-gh)));
+          a.ffn[(size_t)t * kInter + sg.tile * 64 + r] = __float2half_rn(__fmul_rn(silu, uh));
+        }
+      }
+      dev::fence_proxy_async_smem();  // these accesses of ebuf precede any later bulk write into it
+      pw_sync();
+    };
+
     // X slabs by TMA (first phase warp, elected lane 0: the lane that made the
     // barrier's acquire visible to the async proxy), then drains of the
     // finished segments.
@@ -485,7 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       const bool counted = (pi & 3) == 2;
       int last_tiles[4], nlast = 0;
       auto publish = [&](int j) {
-        if (drain(segs[j], T, counted) && nlast < 4) last_tiles[nlast++] = segs[j].tile;
+        if (counted && nslots[pi * kFwdMaxTiles + segs[j].tile] == 1) drain_swiglu(segs[j], T);
+        else if (drain(segs[j], T, counted) && nlast < 4) last_tiles[nlast++] = segs[j].tile;
       };
       for (int j = first; j < si; ++j) {
         const FwdSeg sg = segs[j];

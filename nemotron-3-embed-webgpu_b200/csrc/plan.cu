@@ -114,9 +114,10 @@ int plan_upload(DevicePlan& p, T** ptr, const std::vector<T>& host) {
 }
 
 // Sets up the persistent single-launch forward when the plan's worst case fits
-// kFwdNP tokens (leaves p.fgrid = 0 otherwise). Weight work is split per
-// projection into grid-many contiguous ranges of the tile-major (tile, slab)
-// sequence; a range that crosses a tile boundary becomes two segments. Slots
+// kFwdNP tokens (leaves p.fgrid = 0 otherwise). Weight work of QKV, O and
+// down is split per projection into grid-many contiguous ranges of the
+// tile-major (tile, slab) sequence; a range that crosses a tile boundary
+// becomes two segments. Gate/up tiles are not split (one CTA each). Slots
 // of a tile are numbered in K order, so the partial sums of a tile are always
 // added in the same order. The CTA that takes range 0 rotates per projection
 // so the CTAs with one extra slab differ from projection to projection.
@@ -136,6 +137,10 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   NEMO_CUDA_TRY(cudaDeviceGetAttribute(&G, cudaDevAttrMultiProcessorCount, p.device));
   if (G < 1) return kOk;
 
+  // NEMO_FORWARD_GATE_UP=split: gate/up split over the whole grid like the
+  // other projections (tile counters + SwiGLU by the CTA finishing a tile).
+  const char* gu_env = getenv("NEMO_FORWARD_GATE_UP");
+  const bool split_gate_up = gu_env && strcmp(gu_env, "split") == 0;
   std::vector<std::vector<FwdSeg>> per(G);
   std::vector<uint8_t> nslots((size_t)L * 4 * kFwdMaxTiles, 0);
   int max_slots = 1;
@@ -146,6 +151,32 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
     NEMO_CUDA_TRY(cudaMemcpy(tiles.data(), P.d_tiles, P.tiles * sizeof(SkinnyTile), cudaMemcpyDeviceToHost));
     const long long U = (long long)P.tiles * P.slabs;
     const int rot = (int)(((long long)pi * 37) % G);
+    auto add = [&](int c, int tile, int s0, int s1) -> bool {
+      uint8_t& n = nslots[(size_t)pi * kFwdMaxTiles + tile];
+      if (n == 255) return false;
+      FwdSeg sg = {};
+      sg.chunk0 = P.packed + tiles[tile].offset;
+      sg.chunk_bytes = tiles[tile].chunk_bytes;
+      sg.proj = (uint16_t)pi;
+      sg.tile = (uint16_t)tile;
+      sg.s0 = (uint8_t)s0;
+      sg.s1 = (uint8_t)s1;
+      sg.slot = n++;
+      sg.fmt[0] = tiles[tile].fmt[0];
+      sg.fmt[1] = tiles[tile].fmt[1];
+      max_slots = std::max(max_slots, (int)n);
+      per[c].push_back(sg);
+      return true;
+    };
+    if (pi % 4 == 2 && P.tiles <= G && !split_gate_up) {
+      // Gate/up: every tile whole on one CTA (spread evenly over the grid).
+      // Its SwiGLU epilogue then runs straight from TMEM, with no partial
+      // sums in global memory and no tile counter; the CTAs left over start
+      // decoding their down-projection slabs early.
+      for (int tile = 0; tile < P.tiles; ++tile)
+        if (!add((int)(((long long)tile * G / P.tiles + rot) % G), tile, 0, P.slabs)) return kOk;
+      continue;
+    }
     for (int ce = 0; ce < G; ++ce) {
       const int u0 = (int)(ce * U / G), u1 = (int)((ce + 1) * U / G);
       const int c = (ce + rot) % G;
@@ -154,20 +185,7 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
       for (int u = u0; u < u1;) {
         const int tile = u / P.slabs, s0 = u % P.slabs;
         const int s1 = std::min(P.slabs, s0 + (u1 - u));
-        uint8_t& n = nslots[(size_t)pi * kFwdMaxTiles + tile];
-        if (n == 255) return kOk;
-        FwdSeg sg = {};
-        sg.chunk0 = P.packed + tiles[tile].offset;
-        sg.chunk_bytes = tiles[tile].chunk_bytes;
-        sg.proj = (uint16_t)pi;
-        sg.tile = (uint16_t)tile;
-        sg.s0 = (uint8_t)s0;
-        sg.s1 = (uint8_t)s1;
-        sg.slot = n++;
-        sg.fmt[0] = tiles[tile].fmt[0];
-        sg.fmt[1] = tiles[tile].fmt[1];
-        max_slots = std::max(max_slots, (int)n);
-        per[c].push_back(sg);
+        if (!add(c, tile, s0, s1)) return kOk;
         u += s1 - s0;
       }
     }
