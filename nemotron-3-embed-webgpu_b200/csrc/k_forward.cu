@@ -18,9 +18,12 @@
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
 //               D[128 rows x NP tokens] (+)= A[128 x 64] . X^T[64 x NP] per
 //               substage, D double-buffered in TMEM across segments
-//   warps 2-9   decoders (tile_decode.cuh): warps 2-5 fill substages 0 and 2
-//               of each slab, warps 6-9 substages 1 and 3, into an A ring
-//   warps 10-13 phase warps: the activation side of every phase
+//   warps 2-5   phase warps: the activation side of every phase (below)
+//   warps 6-13  decoders (tile_decode.cuh): warps 6-9 fill substages 0 and 2
+//               of each slab, warps 10-13 substages 1 and 3, into an A ring.
+//               They hold the highest warp numbers of the CTA: with any
+//               higher-numbered warp resident on their scheduler, waiting or
+//               not, the same decoders ran at half the rate (measured).
 //     - projection phases: stage X slabs (f16, 128B-swizzled) into an X
 //       ring, drain each finished segment from TMEM to an f32 partial slot in
 //       global memory, and count the tile's finished segments; the CTA that
@@ -45,7 +48,8 @@ namespace {
 using namespace tsd;
 
 constexpr int kThreads = 448;
-constexpr int kPhaseThread0 = 320;  // warps 10..13
+constexpr int kPhaseThread0 = 64;   // warps 2..5
+constexpr int kDecThread0 = 192;    // warps 6..13
 constexpr int kRawStages = 4;   // packed weight chunks in shared memory
 constexpr int kASlabs = 3;     // decoded A slabs in TMEM (128 x 256 f16 = 128 columns each)
 constexpr int kXStages = 4;
@@ -170,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
   float* rope = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(meta + 1) + 15) & ~(uintptr_t)15);
   int* sstride = reinterpret_cast<int*>(rope + NP * 128);
   uint8_t* nslots = reinterpret_cast<uint8_t*>(sstride + a.n_layers * 4);
+  uint8_t* srank = nslots + a.n_layers * 4 * kFwdMaxTiles;  // [n_layers * 3] this CTA's small-phase ranks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x, G = gridDim.x;
   const int seg0 = a.seg_start[cta];
@@ -185,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     for (int i = threadIdx.x; i < NP * 128; i += kThreads) rope[i] = i < a.rope_rows * 128 ? a.rope[i] : 0.f;
     for (int i = threadIdx.x; i < a.n_layers * 4; i += kThreads) sstride[i] = a.sstride[i];
     for (int i = threadIdx.x; i < a.n_layers * 4 * kFwdMaxTiles; i += kThreads) nslots[i] = a.nslots[i];
+    for (int i = threadIdx.x; i < a.n_layers * 3; i += kThreads) srank[i] = a.small_rank[(size_t)i * G + cta];
   }
 
   if (threadIdx.x == 0) {
@@ -300,12 +306,12 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
     if (dev::elect_one()) dev::tc_commit(fin);
     __syncwarp();
     dev::mbar_wait(fin, 0, err, 100000000ull);
-  } else if (threadIdx.x < kPhaseThread0) {
+  } else if (threadIdx.x >= kDecThread0) {
     // ------------------------------------------------------------ decoders
     // Warp w writes TMEM lanes 32 * (w % 4) .. + 31, so its threads own those
-    // weight rows; warps 2-5 fill substages 0 and 2 of every slab, warps 6-9
+    // weight rows; warps 6-9 fill substages 0 and 2 of every slab, warps 10-13
     // substages 1 and 3. A slab is handed to the MMA once both halves are in.
-    const int quarter = warp & 3, grp = (warp - 2) >> 2;
+    const int quarter = warp & 3, grp = (warp - kDecThread0 / 32) >> 2;
     const int r = quarter * 32 + lane;
     const int half = r >> 6, rr = r & 63;  // half is uniform within a warp
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -336,9 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
           break;
         }
         // Both quarters are decoded into separate registers before either
-        // TMEM store: the two independent chains fill the issue slots of the
-        // two decoder warps per scheduler (one quarter at a time, each store
-        // waiting on its source registers, ran at a third of that rate).
+        // TMEM store (two independent chains per thread).
         {
           uint32_t ha[32], hb[32];
           const RegSink sa{ha}, sb{hb};
@@ -633,10 +637,11 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
       if (pt == 0) *reinterpret_cast<volatile int*>(&sh->quiet) = on ? 1 : 0;
     };
     // Only CTAs that hold items quiet their decoders: the others keep the
-    // weight rings filling through the small phases.
-    auto norm_phase = [&](__half* x, int rpi, const float* w, __half* out, int T) {
-      if (cta < T) set_quiet(true);
-      for (int t = cta; t < T; t += G) norm_row(x, rpi, w, out, t);
+    // weight rings filling through the small phases. Items go to CTAs by
+    // rank (the least work in the next projection first).
+    auto norm_phase = [&](__half* x, int rpi, const float* w, __half* out, int T, int rank) {
+      if (rank < T) set_quiet(true);
+      for (int t = rank; t < T; t += G) norm_row(x, rpi, w, out, t);
       set_quiet(false);
     };
 
@@ -784,8 +789,9 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         float* linv = ps + 8 * NP;                     // [8]
         const int* off = merged ? meta->tgt_off : meta->src_off;
         constexpr int kQG = 8, kGroups = (NP + kQG - 1) / kQG;
-        if (cta < batch * kQHeads * kGroups) set_quiet(true);
-        for (int item = cta; item < batch * kQHeads * kGroups; item += G) {
+        const int rank = srank[l * 3];
+        if (rank < batch * kQHeads * kGroups) set_quiet(true);
+        for (int item = rank; item < batch * kQHeads * kGroups; item += G) {
           const int b = item / (kQHeads * kGroups), rem = item % (kQHeads * kGroups);
           const int h = rem / kGroups, g = rem % kGroups, kvh = h / (kQHeads / kKVHeads);
           const int len = min(merged ? meta->tgt_len[b] : meta->src_len[b], NP);
@@ -880,13 +886,13 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
 
       projection(l * 4 + 1, &a.xmap[2], merged);
       grid_barrier();
-      norm_phase(X, l * 4 + 1, a.ffn_norm[l], N, T);
+      norm_phase(X, l * 4 + 1, a.ffn_norm[l], N, T, srank[l * 3 + 1]);
       grid_barrier();
       projection(l * 4 + 2, &a.xmap[merged ? 1 : 0], merged);
       grid_barrier();
       projection(l * 4 + 3, &a.xmap[3], merged);
       grid_barrier();
-      norm_phase(X, l * 4 + 3, l + 1 < a.n_layers ? a.attn_norm[l + 1] : a.output_norm, N, T);
+      norm_phase(X, l * 4 + 3, l + 1 < a.n_layers ? a.attn_norm[l + 1] : a.output_norm, N, T, srank[l * 3 + 2]);
       grid_barrier();
     }
 
@@ -954,7 +960,7 @@ size_t forward_smem_bytes(int chunk_max, int scratch_slots, int max_segs, int n_
   return 1024 + (size_t)kXStages * kXBytes + (size_t)scratch_slots * kFwdNP * 128 * 4 +
          (((size_t)kRawStages * chunk_max + 15) & ~15) + 8 * (2 * kRawStages + 2 * kASlabs + 2 * kXStages + 7) +
          ((sizeof(Shared) + 15) & ~15) + (size_t)max_segs * sizeof(FwdSeg) + sizeof(Meta) + 16 + kFwdNP * 128 * 4 +
-         (size_t)n_layers * 4 * (4 + kFwdMaxTiles);
+         (size_t)n_layers * 4 * (4 + kFwdMaxTiles) + (size_t)n_layers * 3;
 }
 
 cudaError_t launch_forward(const FwdArgs& a, int grid, cudaStream_t s) {

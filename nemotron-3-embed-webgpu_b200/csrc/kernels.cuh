@@ -305,6 +305,10 @@ struct FwdArgs {
   const FwdSeg* segs;       // per-CTA lists in forward order, concatenated
   const int* seg_start;     // [grid + 1]
   const uint8_t* nslots;    // [n_layers * 4][kFwdMaxTiles]
+  const uint8_t* small_rank;  // [n_layers * 3][grid]: a CTA's place in the attention, post-attention
+                              // norm and post-FFN norm item lists of each layer (least next-projection
+                              // work first, so the CTAs that pause their decoders for these phases
+                              // have the least weight work right after them)
   uint32_t* sync;           // [0] grid barrier, [1 + proj * kFwdMaxTiles + tile] tile counters; zero at launch
   uint32_t* err;
   const uint32_t* ids;      // [batch x seq]

@@ -190,6 +190,26 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
       }
     }
   }
+  // Items of the small phases that pause their CTA's decoders (attention and
+  // the two norms of each layer) go first to the CTAs with the fewest slabs in
+  // the projection that follows the phase.
+  if (G > 255) return kOk;
+  std::vector<uint8_t> small_rank((size_t)L * 3 * G, 0);
+  {
+    std::vector<int> order(G);
+    for (int l = 0; l < L; ++l)
+      for (int k = 0; k < 3; ++k) {
+        const int next = k == 0 ? l * 4 + 1 : k == 1 ? l * 4 + 2 : (l + 1 < L ? (l + 1) * 4 : -1);
+        std::vector<int> load(G, 0);
+        if (next >= 0)
+          for (int c = 0; c < G; ++c)
+            for (const FwdSeg& sg : per[c])
+              if (sg.proj == next) load[c] += sg.s1 - sg.s0;
+        for (int c = 0; c < G; ++c) order[c] = c;
+        std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return load[x] < load[y]; });
+        for (int i = 0; i < G; ++i) small_rank[((size_t)l * 3 + k) * G + order[i]] = (uint8_t)i;
+      }
+  }
   std::vector<FwdSeg> segs;
   std::vector<int> start(G + 1, 0);
   int max_segs = 1;
@@ -222,8 +242,9 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   FwdSeg* d_segs = nullptr;
   int* d_start = nullptr;
   uint8_t* d_nslots = nullptr;
+  uint8_t* d_small = nullptr;
   if (plan_upload(p, &d_sstride, sstride) || plan_upload(p, &d_segs, segs) || plan_upload(p, &d_start, start) ||
-      plan_upload(p, &d_nslots, nslots))
+      plan_upload(p, &d_nslots, nslots) || plan_upload(p, &d_small, small_rank))
     return kErrCuda;
   p.fsync_bytes = (size_t)(1 + L * 4 * kFwdMaxTiles) * 4;
   if (plan_alloc(p, &p.fsync, p.fsync_bytes) ||
@@ -233,6 +254,7 @@ int setup_forward(nemo_model* m, DeviceModel* dm, DevicePlan& p) {
   a.segs = d_segs;
   a.seg_start = d_start;
   a.nslots = d_nslots;
+  a.small_rank = d_small;
   a.sync = p.fsync;
   a.err = p.err;
   a.ids = p.ids;
