@@ -232,41 +232,65 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         break;
       }
       dev::tc_fence_after();
-      // the row's four 32-column loads are all in flight before one wait
-      uint32_t sr[kTile];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        dev::tmem_ld_32x32b_x32(lane_base + colS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      dev::tc_wait_ld();
-      float s[kTile];
-#pragma unroll
-      for (int i = 0; i < kTile; ++i) s[i] = __uint_as_float(sr[i]);
       const int valid = min(kTile, nkeys - j * kTile);
-      // The max of the raw scores, scaled once (scale > 0 keeps the order).
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < kTile; ++i) {
-        s[i] = i < valid ? s[i] : -INFINITY;
-        tmax = fmaxf(tmax, s[i]);
-      }
-      tmax *= scale;
+      // The S row: its four 32-column loads in flight before one wait; keys
+      // past the valid ones (only on a partial last tile) masked to -inf.
+      // (A macro, not a lambda: s must stay in registers.)
+#define NEMO_LOAD_S_ROW()                                                                                  \
+  do {                                                                                                     \
+    _Pragma("unroll") for (int c = 0; c < 4; ++c)                                                          \
+        dev::tmem_ld_32x32b_x32(lane_base + colS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32])); \
+    dev::tc_wait_ld();                                                                                     \
+    if (valid < kTile) {                                                                                   \
+      _Pragma("unroll") for (int i = 0; i < kTile; ++i) s[i] = i < valid ? s[i] : -INFINITY;               \
+    }                                                                                                      \
+  } while (0)
+      float s[kTile];
+      NEMO_LOAD_S_ROW();
       // The running max of the warp's rows moves only when some row's tile
       // max exceeds it by more than kMaxSlack (log2 units). Otherwise P is
       // taken against the stale max: P <= 2^kMaxSlack, well inside f16, and
       // O / l is unchanged, while the O rows need no rescale on that tile.
       // (With the exact running max nearly every tile moves some row's max.)
-      const bool move = __any_sync(0xffffffffu, tmax > m + kMaxSlack);  // always on the first tile
-      const float mnew = move ? fmaxf(m, tmax) : m;
-      // p = 2^(s * scale - mnew): one FMA per score on the raw value.
-      const float nm = -mnew;
-      float rs0 = 0.f, rs1 = 0.f;  // two independent sum chains
+      // From the second tile on the exponentials are computed against the
+      // running max straight after the load, the tile max (of the raw scores,
+      // scaled once: scale > 0 keeps the order) beside them; only when the max
+      // moves is the row reloaded from TMEM (P has not overwritten it yet) and
+      // recomputed against the new max. On the first tile the max always moves.
+      // p = 2^(s * scale - m): one FMA per score on the raw value.
+      float tmax = -INFINITY, rs0 = 0.f, rs1 = 0.f;  // two independent sum chains
+      bool move = true;
+      if (j > 0) {
+        const float nm = -m;
 #pragma unroll
-      for (int i = 0; i < kTile; i += 2) {
-        s[i] = ex2(fmaf(s[i], scale, nm));
-        s[i + 1] = ex2(fmaf(s[i + 1], scale, nm));
-        rs0 += s[i];
-        rs1 += s[i + 1];
+        for (int i = 0; i < kTile; i += 2) {
+          tmax = fmaxf(tmax, fmaxf(s[i], s[i + 1]));
+          s[i] = ex2(fmaf(s[i], scale, nm));
+          s[i + 1] = ex2(fmaf(s[i + 1], scale, nm));
+          rs0 += s[i];
+          rs1 += s[i + 1];
+        }
+        tmax *= scale;
+        move = __any_sync(0xffffffffu, tmax > m + kMaxSlack);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) tmax = fmaxf(tmax, s[i]);
+        tmax *= scale;
       }
+      const float mnew = move ? fmaxf(m, tmax) : m;
+      if (move) {
+        if (j > 0) NEMO_LOAD_S_ROW();
+        const float nm = -mnew;
+        rs0 = rs1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < kTile; i += 2) {
+          s[i] = ex2(fmaf(s[i], scale, nm));
+          s[i + 1] = ex2(fmaf(s[i + 1], scale, nm));
+          rs0 += s[i];
+          rs1 += s[i + 1];
+        }
+      }
+#undef NEMO_LOAD_S_ROW
       const float rsum = rs0 + rs1;
       const float alpha = ex2(m - mnew);  // 0 on the first tile, 1 while the max stays
       // P_t (f16) over its own S columns: S_t(j) has been read, and neither

@@ -127,6 +127,35 @@ def test_single_launch_forward(models, lengths, monkeypatch):
         assert cosine(got[b], base[b]) >= FUSED_VS_PER_OP, b
 
 
+@pytest.mark.parametrize("lengths", [[15], [3, 4, 2, 1]])
+def test_single_launch_split_gate_up(models, lengths, monkeypatch):
+    """NEMO_FORWARD_GATE_UP=split spreads gate/up over the whole grid (tile
+    counters, SwiGLU by the CTA finishing a tile last) instead of one CTA per
+    tile; both schedules give the per-op embeddings."""
+    _, gpu, orc = models
+    reqs = synth.make_requests(29, lengths, vocab=orc.vocab)
+    ids, lens, seq = synth.pad_batch(reqs)
+    whole = gpu.create_plan(len(lengths), seq)
+    with monkeypatch.context() as m:
+        m.setenv("NEMO_FORWARD_GATE_UP", "split")
+        split = gpu.create_plan(len(lengths), seq)
+    ref = per_op_plan(gpu, len(lengths), seq, monkeypatch)
+    try:
+        assert whole.fused and split.fused and not ref.fused
+        a = whole.run_array(ids, lens).copy()
+        b = split.run_array(ids, lens).copy()
+        again = split.run_array(ids, lens).copy()
+        base = ref.run_array(ids, lens).copy()
+    finally:
+        whole.destroy()
+        split.destroy()
+        ref.destroy()
+    assert np.array_equal(b, again)
+    for i in range(len(lengths)):
+        assert cosine(a[i], base[i]) >= FUSED_VS_PER_OP, i
+        assert cosine(b[i], base[i]) >= FUSED_VS_PER_OP, i
+
+
 def test_single_launch_only_for_small_plans(models):
     _, gpu, _ = models
     small, large = gpu.create_plan(2, 8), gpu.create_plan(2, 9)
