@@ -54,13 +54,6 @@ namespace {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-int pick_bn(int rows, int n) {
-  const int mt = (rows + kGemmTileM - 1) / kGemmTileM;
-  if ((long long)mt * (n / 256) >= 148) return 2;
-  if ((long long)mt * (n / 128) >= 148) return 1;
-  return 0;
-}
-
 int merged_len(int s) { return std::max(1, (int)ceil(s * 0.64)); }
 
 Meta make_meta(int len0, int len1, int seq) {

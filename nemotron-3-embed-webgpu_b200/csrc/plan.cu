@@ -87,13 +87,6 @@ int stage_test_stall(DevicePlan& p) {
   return kOk;
 }
 
-int pick_bn(int rows, int n) {
-  const int mt = (rows + kGemmTileM - 1) / kGemmTileM;
-  if ((long long)mt * (n / 256) >= 148) return 2;
-  if ((long long)mt * (n / 128) >= 148) return 1;
-  return 0;
-}
-
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 template <typename T>
