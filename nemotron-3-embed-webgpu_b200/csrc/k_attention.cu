@@ -83,15 +83,20 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict
     for (int i = 0; i < 8; ++i) {
       const int qi = warp * 8 + i;
       if (q0 + qi >= len) continue;
-      float s = 0.f;
+      // four independent partial sums (dimensions d mod 4), added at the end
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
       for (int d = 0; d < kHeadDim; d += 4) {
         const float4 kk = *reinterpret_cast<const float4*>(&ks[lane][d]);
         const __half2 qa = *reinterpret_cast<const __half2*>(&qs[qi][d]);
         const __half2 qb = *reinterpret_cast<const __half2*>(&qs[qi][d + 2]);
         const float2 fa = __half22float2(qa), fb = __half22float2(qb);
-        s += fa.x * kk.x + fa.y * kk.y + fb.x * kk.z + fb.y * kk.w;
+        s4[0] = fmaf(fa.x, kk.x, s4[0]);
+        s4[1] = fmaf(fa.y, kk.y, s4[1]);
+        s4[2] = fmaf(fb.x, kk.z, s4[2]);
+        s4[3] = fmaf(fb.y, kk.w, s4[3]);
       }
+      float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       s = key_valid ? s * scale * temp[i] : -INFINITY;
       float tmax = s;
 #pragma unroll

@@ -251,8 +251,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(__half* x, const __half* _
 
 // rmsnorm_kernel after a GEMM launched with GemmEpi::part: when that GEMM
 // split K, the residual is f16(its f32 parts summed in split order), the f16
-// projection output an unsplit GEMM stores; otherwise its f16 output.
-__global__ void __launch_bounds__(256, 8) rmsnorm_parts_kernel(__half* x, const __half* __restrict__ residual,
+// projection output an unsplit GEMM stores; otherwise its f16 output. One
+// block per row. WIDE issues every split's loads before the first add (one
+// round trip instead of one per split) at the cost of registers (2 blocks per
+// SM): the launcher takes it when the plan's rows are few, which is also when
+// the GEMM splits K.
+template <bool WIDE>
+__global__ void __launch_bounds__(256, WIDE ? 2 : 8) rmsnorm_parts_kernel(__half* x, const __half* __restrict__ residual,
                                                             const float* __restrict__ part,
                                                             const int* __restrict__ d_splits,
                                                             const float* __restrict__ w, __half* norm,
@@ -272,6 +277,28 @@ __global__ void __launch_bounds__(256, 8) rmsnorm_parts_kernel(__half* x, const 
   float r[8];
   if (splits == 1) {
     unpack8(rv, r);
+  } else if (WIDE) {
+    float4 pa[kMaxKSplit], pb[kMaxKSplit];
+#pragma unroll
+    for (int sp = 0; sp < kMaxKSplit; ++sp) {
+      if (sp < splits) {
+        const float4* p = reinterpret_cast<const float4*>(part + ((size_t)sp * M + row) * kHidden + c);
+        pa[sp] = __ldcg(p);
+        pb[sp] = __ldcg(p + 1);
+      }
+    }
+    r[0] = pa[0].x, r[1] = pa[0].y, r[2] = pa[0].z, r[3] = pa[0].w;
+    r[4] = pb[0].x, r[5] = pb[0].y, r[6] = pb[0].z, r[7] = pb[0].w;
+#pragma unroll
+    for (int sp = 1; sp < kMaxKSplit; ++sp) {
+      if (sp < splits) {
+        const float u[8] = {pa[sp].x, pa[sp].y, pa[sp].z, pa[sp].w, pb[sp].x, pb[sp].y, pb[sp].z, pb[sp].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = __fadd_rn(r[i], u[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = __half2float(__float2half_rn(r[i]));
   } else {
     {
       const float4* p = reinterpret_cast<const float4*>(part + (size_t)row * kHidden + c);
@@ -519,7 +546,12 @@ cudaError_t launch_residual_rmsnorm_parts(__half* x, const __half* residual, con
                                           const float* w, __half* norm, const int* d_rows, int max_rows,
                                           cudaStream_t s) {
   if (!residual || !part || !d_splits) return cudaErrorInvalidValue;
-  rmsnorm_parts_kernel<<<max_rows, 256, 0, s>>>(x, residual, part, d_splits, w, norm, d_rows, kEpsilon);
+  // (1280 rows: 10 row tiles, the most at which the O / down GEMMs still
+  // split K by 8 on 148 SMs)
+  if (max_rows <= 1280)
+    rmsnorm_parts_kernel<true><<<max_rows, 256, 0, s>>>(x, residual, part, d_splits, w, norm, d_rows, kEpsilon);
+  else
+    rmsnorm_parts_kernel<false><<<max_rows, 256, 0, s>>>(x, residual, part, d_splits, w, norm, d_rows, kEpsilon);
   return cudaGetLastError();
 }
 

@@ -194,11 +194,12 @@ struct GemmEpi {
 // of tiles no split is taken: at 200-320 tiles (one 3200-5000-token request)
 // splitting in two saved less in the GEMMs than the norms spent on partials.
 // Host and device evaluate the same integers.
+constexpr int kMaxKSplit = 8;  // most K splits gemm_ksplit picks
 __host__ __device__ inline int gemm_ksplit(int m_tiles, int n_tiles, int kt, int g) {
   const int tiles = m_tiles * n_tiles;
   if (tiles <= 0 || g <= 0 || kt <= 0 || tiles >= g) return 1;
   int best = 1, best_cost = 0x7fffffff;
-  for (int s = 1; s <= 8 && kt / s >= 4; ++s) {
+  for (int s = 1; s <= kMaxKSplit && kt / s >= 4; ++s) {
     const int waves = (tiles * s + g - 1) / g;
     const int cost = waves * (1000 / s + 50) + (s > 1 ? s * m_tiles * 355 / kt : 0);
     if (cost < best_cost) {
