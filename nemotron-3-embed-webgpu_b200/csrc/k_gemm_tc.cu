@@ -7,17 +7,21 @@
 //
 // Persistent: one CTA per SM walks its 128 x BN output tiles; two TMEM
 // accumulators let the epilogue of one tile overlap the MMAs of the next.
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      TMA producer: 64-wide K slabs of A (128 x 64) and B (BN x 64)
 //               into a STAGES-deep ring that runs on across tiles, 128-byte
 //               swizzled, mbarrier complete_tx
 //   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16 per
 //               instruction; converged warp, elected lane), tcgen05.commit
 //               frees each stage
-//   warps 2..5  epilogue: tcgen05.ld 32x32b (one row per thread), then an f16
+//   warps 2..9  epilogue: tcgen05.ld 32x32b (one row per thread), then an f16
 //               store, RoPE (QKV: Q/K pairs rotated into the attention
 //               inputs, ops.ts:168-194) or SwiGLU (gate/up: the B tile holds
-//               BN/2 gate rows then the matching BN/2 up rows, ops.ts:74-89)
+//               BN/2 gate rows then the matching BN/2 up rows, ops.ts:74-89).
+//               Warps 2-5 take the first half of the tile's columns, warps
+//               6-9 (same TMEM lane quarters) the second: with one tile per
+//               CTA (few tokens) nothing overlaps the epilogue, so its length
+//               is on the critical path.
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error word,
 // drains what this CTA has in flight and frees its TMEM before returning.
 #include <cudaTypedefs.h>
@@ -70,7 +74,7 @@ __device__ __forceinline__ void plain_pack(const uint32_t (&r)[32], uint32_t (&o
 // Persistent: CTA c takes tiles c, c + grid, ... of the (m tile, n tile)
 // grid in n-fastest order; M (valid token rows) is read on the device.
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, __half* y,
                    int ldy, const int* __restrict__ d_rows, int k, int n_tiles, uint32_t* err, GemmEpi e) {
   using C = GemmCfg<BN>;
@@ -104,7 +108,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       dev::mbar_init(tfull + 8 * b, 1);
-      dev::mbar_init(tempty + 8 * b, 128);
+      dev::mbar_init(tempty + 8 * b, 256);
     }
     dev::mbar_init(fin, 1);
     dev::fence_mbar_init();
@@ -192,8 +196,8 @@ __global__ void __launch_bounds__(192, 1)
     // All MMAs of this CTA have retired before TMEM is released below.
     dev::mbar_wait(fin, 0, err, 100000000ull);
   } else {
-    const int quarter = warp & 3;
-    uint8_t* stage = smem + C::STAGES * C::STAGE_BYTES + 256 + quarter * (32 * 128);
+    const int quarter = warp & 3, group = (warp - 2) >> 2;
+    uint8_t* stage = smem + C::STAGES * C::STAGE_BYTES + 256 + quarter * (32 * 128);  // group 0 only
     int i = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
       const int buf = i & 1;
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(192, 1)
       if (e.mode == kSkinnySwiglu) {
         // out[row][g] = f16(silu(f16 gate) * f16 up) for the tile's BN/2 outputs
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = group * (BN / 4); c < (group + 1) * (BN / 4); c += 32) {
           uint32_t g[32], u[32];
           dev::tmem_ld_32x32b_x32(tbase + c, g);
           dev::tmem_ld_32x32b_x32(tbase + BN / 2 + c, u);
@@ -252,10 +256,14 @@ __global__ void __launch_bounds__(192, 1)
             for (int v = 0; v < 8; ++v) cs[v] = __ldg(src + v);
           }
         };
+        // 32-column chunks of this warp's group; a head-parallel run's staged
+        // peer stores pair chunks, so group 0 takes the whole tile there.
+        const int c0 = e.hp.n_dev ? (group ? BN / 32 : 0) : group * (BN / 64);
+        const int c1 = e.hp.n_dev ? BN / 32 : (group + 1) * (BN / 64);
         float4 cs_cur[8], cs_nxt[8];
-        load_cs(0, cs_cur);
+        load_cs(c0, cs_cur);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = c0; c < c1; ++c) {
           const int col0 = n0 + c * 32;
           uint32_t r[32];
           dev::tmem_ld_32x32b_x32(tbase + c * 32, r);
@@ -375,7 +383,7 @@ cudaError_t launch_bn(const CUtensorMap* ma, const CUtensorMap* mb, __half* y, i
   const long long tiles = (long long)((max_rows + C::BM - 1) / C::BM) * n_tiles;
   // With K-split partial sums every SM takes units (gemm_ksplit sees the grid).
   const int grid = ep.part ? sms[dev] : (int)std::min<long long>(sms[dev], std::max<long long>(tiles, 1));
-  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, n_tiles, err, ep);
+  gemm_tc_kernel<BN><<<grid, 320, C::SMEM, s>>>(*ma, *mb, y, ldy, d_rows, k, n_tiles, err, ep);
   return cudaGetLastError();
 }
 
