@@ -34,10 +34,19 @@ namespace {
 constexpr int kTile = 128;
 constexpr int kHalfTile = kTile * 64 * 2;  // 128 rows x 64 f16 = 16 KB (one 128B-swizzle column block)
 constexpr int kTileBytes = 2 * kHalfTile;  // 128 x 128 f16
-constexpr int kThreadsA = 320;
-constexpr int kSmem = 1024 + 2 * kTileBytes /*Q_0, Q_1*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ + 256;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 256;  // S_t at kColS + 128 t, O_t at kColO + 128 t
+// Two shapes of the kernel: NT query tiles per CTA sharing every K/V tile,
+// KVS K/V stages. <2, 2> (320 threads, 512 TMEM columns, ~197 KB) for long
+// requests; <1, 1> (192 threads, 256 TMEM columns, ~97 KB, two CTAs per SM)
+// for plans of short requests, whose one or two key tiles leave nothing to
+// pipeline and whose CTAs are mostly set-up: a second resident CTA overlaps it.
+template <int NT, int KVS>
+struct AttnCfg {
+  static constexpr int kThreads = 64 + 128 * NT;
+  static constexpr int kSmem = 1024 + NT * kTileBytes /*Q*/ + KVS * kTileBytes /*K*/ + KVS * kTileBytes /*V*/ + 256;
+  static constexpr uint32_t kTmemCols = 256 * NT;
+  static constexpr uint32_t kColS = 0, kColO = 128 * NT;  // S_t at kColS + 128 t, O_t at kColO + 128 t
+};
+constexpr int kShortAttentionMaxLen = 256;  // plans up to this many rows use AttnCfg<1, 1>
 constexpr float kMaxSlack = 8.0f;           // running-max hysteresis (log2 units): P <= 256
 
 __device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
@@ -61,19 +70,22 @@ struct AttnTcArgs {
   AttnScatter scatter;  // scatter.dst[0] set: rows go to the devices that own them
 };
 
-__global__ void __launch_bounds__(kThreadsA, 1)
+template <int NT, int KVS>
+__global__ void __launch_bounds__(AttnCfg<NT, KVS>::kThreads, NT == 1 ? 2 : 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_kc,
                         const __grid_constant__ CUtensorMap map_vc, AttnTcArgs a) {
+  using C = AttnCfg<NT, KVS>;
+  constexpr uint32_t kColS = C::kColS, kColO = C::kColO;
   extern __shared__ uint8_t smem_raw[];
   dev::pdl_launch_dependents();
-  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * 2 * kTile;
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * NT * kTile;
   const Meta* meta = a.meta;
   if (b >= meta->batch) return;
   const int ph = a.merged ? 1 : 0;
   const int len = a.merged ? meta->tgt_len[b] : meta->src_len[b];
   if (q0 >= len) return;  // uniform over the CTA
-  const int nqt = q0 + kTile < len ? 2 : 1;  // query tiles with valid rows
+  const int nqt = NT == 2 && q0 + kTile < len ? 2 : 1;  // query tiles with valid rows
   const int base = a.merged ? meta->tgt_off[b] : meta->src_off[b];
   const int kvh = h / (kQHeads / kKVHeads);
   const bool sampled = !meta->exact && len > kSampleThreshold;
@@ -87,10 +99,10 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 
   const uint32_t raw_s = dev::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
-  uint8_t* sQ = smem;                    // Q_0, Q_1
-  uint8_t* sK = sQ + 2 * kTileBytes;
-  uint8_t* sV = sK + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
+  uint8_t* sQ = smem;                    // Q_0 (, Q_1)
+  uint8_t* sK = sQ + NT * kTileBytes;
+  uint8_t* sV = sK + KVS * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KVS * kTileBytes);
   const uint32_t q_full = dev::smem_u32(bars);
   const uint32_t kv_full = q_full + 8, kv_empty = kv_full + 16;
   const uint32_t s_full = kv_empty + 16, p_ready = s_full + 16, pv_done = p_ready + 16;
@@ -114,7 +126,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     dev::fence_mbar_init();
   }
   if (warp == 1) {
-    dev::tmem_alloc(dev::smem_u32(tmem_slot), kTmemCols);
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), C::kTmemCols);
     dev::tmem_relinquish();
   }
   dev::tc_fence_before();
@@ -136,8 +148,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     __syncwarp();
     int issued = 0;
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j & 1;
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_empty + 8 * st, ((j >> 1) & 1) ^ 1, a.err))) break;
+      const int st = j % KVS;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_empty + 8 * st, ((j / KVS) & 1) ^ 1, a.err))) break;
       const uint32_t fb = kv_full + 8 * st;
       const uint32_t dk = dev::smem_u32(sK + st * kTileBytes), dv = dev::smem_u32(sV + st * kTileBytes);
       const int row = kbase + j * kTile;
@@ -152,8 +164,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       ++issued;
     }
     dev::mbar_wait(q_full, 0, a.err, 100000000ull);
-    for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
-      dev::mbar_wait(kv_full + 8 * (i & 1), (i >> 1) & 1, a.err, 100000000ull);
+    for (int i = issued > KVS ? issued - KVS : 0; i < issued; ++i)
+      dev::mbar_wait(kv_full + 8 * (i % KVS), (i / KVS) & 1, a.err, 100000000ull);
   } else if (warp == 1) {
     // Converged warp; the elected lane (lane 0) issues every MMA and commit.
     // Order per key tile j and query tile t: PV_t(j-1) (reads P_t from the
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     auto pv = [&](int t, int jj) -> bool {  // O_t += P_t(jj) . V(jj)
       if (!__all_sync(0xffffffffu, dev::mbar_wait(p_ready + 8 * t, jj & 1, a.err))) return false;
       dev::tc_fence_after();
-      const uint32_t bv = dev::smem_u32(sV + (jj & 1) * kTileBytes);
+      const uint32_t bv = dev::smem_u32(sV + (jj % KVS) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
         if (dev::elect_one()) {
@@ -181,7 +193,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     };
     auto qk = [&](int t, int j) {  // S_t = Q_t . K(j)^T
       const uint32_t aq = dev::smem_u32(sQ + t * kTileBytes);
-      const uint32_t bk = dev::smem_u32(sK + (j & 1) * kTileBytes);
+      const uint32_t bk = dev::smem_u32(sK + (j % KVS) * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kHeadDim / 16; ++kk) {
         if (dev::elect_one()) {
@@ -194,21 +206,38 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       if (dev::elect_one()) dev::tc_commit(s_full + 8 * t);
       __syncwarp();
     };
-    for (int j = 0; j < ntiles && ok; ++j) {
-      if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full + 8 * (j & 1), (j >> 1) & 1, a.err))) {
-        ok = false;
-        break;
+    if (KVS == 1) {
+      // One K/V stage: K/V tile j + 1 is loaded only after P.V(j) has read
+      // V(j), so each key tile runs S, softmax, P.V in turn.
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full, j & 1, a.err))) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        for (int t = 0; t < nqt; ++t) qk(t, j);
+        for (int t = 0; t < nqt && ok; ++t) ok = pv(t, j);
+        // every MMA that reads the key/value stage has been issued
+        if (ok && dev::elect_one()) dev::tc_commit(kv_empty);
+        __syncwarp();
       }
-      dev::tc_fence_after();
-      for (int t = 0; t < nqt && ok; ++t) {
-        if (j > 0) ok = pv(t, j - 1);
-        if (ok) qk(t, j);
+    } else {
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (!__all_sync(0xffffffffu, dev::mbar_wait(kv_full + 8 * (j % KVS), (j / KVS) & 1, a.err))) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        for (int t = 0; t < nqt && ok; ++t) {
+          if (j > 0) ok = pv(t, j - 1);
+          if (ok) qk(t, j);
+        }
+        // every MMA that reads key/value stage j - 1 has been issued
+        if (ok && j > 0 && dev::elect_one()) dev::tc_commit(kv_empty + 8 * ((j - 1) % KVS));
+        __syncwarp();
       }
-      // every MMA that reads key/value stage j - 1 has been issued
-      if (ok && j > 0 && dev::elect_one()) dev::tc_commit(kv_empty + 8 * ((j - 1) & 1));
-      __syncwarp();
+      for (int t = 0; t < nqt && ok; ++t) ok = pv(t, ntiles - 1);
     }
-    for (int t = 0; t < nqt && ok; ++t) ok = pv(t, ntiles - 1);
     if (dev::elect_one()) dev::tc_commit(mma_fin);
     __syncwarp();
     dev::mbar_wait(mma_fin, 0, a.err, 100000000ull);  // every MMA retired before TMEM is freed
@@ -389,7 +418,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   __syncthreads();
   if (warp == 1) {
     dev::tc_fence_after();
-    dev::tmem_dealloc(tmem, kTmemCols);
+    dev::tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -447,20 +476,36 @@ cudaError_t launch_attention_tc_group(const AttnMaps& maps, const Meta* meta, bo
   if (scatter && (batch != 1 || scatter->n_dev < 1 || scatter->n_dev > 8 || scatter->rows_per_dev < 1 ||
                   scatter->col0 % 8 || !scatter->dst[0]))
     return cudaErrorInvalidValue;
-  static bool configured[64] = {};
+  static bool configured[64][2] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  // NEMO_ATTENTION_SHORT_MAX overrides the row bound of the short shape
+  static const int short_max = [] {
+    const char* v = getenv("NEMO_ATTENTION_SHORT_MAX");
+    return v && *v ? atoi(v) : kShortAttentionMaxLen;
+  }();
+  const bool shrt = max_len <= short_max;
+  if (!configured[dev][shrt]) {
+    e = shrt ? cudaFuncSetAttribute(attention_tc_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    AttnCfg<1, 1>::kSmem)
+             : cudaFuncSetAttribute(attention_tc_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    AttnCfg<2, 2>::kSmem);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev][shrt] = true;
   }
   AttnTcArgs a{meta, merged ? 1 : 0, out, err, v_col0, out_ld, {}};
   if (scatter) a.scatter = *scatter;
-  dim3 grid((max_len + 2 * kTile - 1) / (2 * kTile), q_heads, batch);
-  attention_tc_kernel<<<grid, kThreadsA, kSmem, s>>>(maps.q, maps.k, maps.v, maps.kc, maps.vc, a);
+  if (shrt) {
+    dim3 grid((max_len + kTile - 1) / kTile, q_heads, batch);
+    attention_tc_kernel<1, 1><<<grid, AttnCfg<1, 1>::kThreads, AttnCfg<1, 1>::kSmem, s>>>(maps.q, maps.k, maps.v,
+                                                                                        maps.kc, maps.vc, a);
+  } else {
+    dim3 grid((max_len + 2 * kTile - 1) / (2 * kTile), q_heads, batch);
+    attention_tc_kernel<2, 2><<<grid, AttnCfg<2, 2>::kThreads, AttnCfg<2, 2>::kSmem, s>>>(maps.q, maps.k, maps.v,
+                                                                                        maps.kc, maps.vc, a);
+  }
   return cudaGetLastError();
 }
 
