@@ -27,7 +27,6 @@ struct Meta {
 };
 
 constexpr int kSampleThreshold = 2048;
-constexpr int kSimtAttentionMaxLen = 64;  // plans whose requests are this short use the CUDA-core attention
 constexpr int kSampleStride = 3;
 
 // Weight segment formats accepted by the decoders.

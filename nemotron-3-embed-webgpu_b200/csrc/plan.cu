@@ -414,12 +414,8 @@ int enqueue_forward(DevicePlan& p, int n_layers, cudaStream_t s, Profile* prof, 
         NEMO_LAUNCH(launch_rope(p.qkv, p.rope, p.meta, merged, maxr, p.q, p.k, s));
       }
     }
-    if (p.simt_attention) {
-      NEMO_LAUNCH(launch_attention(p.q, p.k, p.qkv, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, s));
-    } else {
-      if (p.gather[ph]) NEMO_LAUNCH(launch_gather_sampled(p.k, p.qkv, p.meta, merged, p.rows_c, p.kc, p.vc, s));
-      NEMO_LAUNCH(launch_attention_tc(p.amaps, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, p.err, s));
-    }
+    if (p.gather[ph]) NEMO_LAUNCH(launch_gather_sampled(p.k, p.qkv, p.meta, merged, p.rows_c, p.kc, p.vc, s));
+    NEMO_LAUNCH(launch_attention_tc(p.amaps, p.meta, merged, p.cap_batch, merged ? p.mseq : p.seq, p.attn, p.err, s));
     stage(4);
     if (np) {
       if (int rc = skinny(kProjO, &p.xmap_attn[ph], kSkinnyPlain, p.delta, kHidden)) return rc;
@@ -580,15 +576,6 @@ int create_device_plan(nemo_model* m, DeviceModel* dm, int cap_batch, int seq, b
       make_tmap_f16(&p.map_ffn, p.ffn, kInter, r0, 64, kGemmTileM))
     return kErrCuda;
   // Attention: compact sampled K/V only when a phase can exceed 2048 keys.
-  // Requests of at most kSimtAttentionMaxLen tokens: the CUDA-core attention
-  // (one block per 32 queries, head and request) instead of the tcgen05 kernel,
-  // whose CTAs (256 queries, TMEM allocation, K/V TMA ring) are mostly idle on
-  // a handful of keys. NEMO_ATTENTION_SIMT_MAX overrides the bound.
-  {
-    int simt_max = kSimtAttentionMaxLen;
-    if (const char* e = getenv("NEMO_ATTENTION_SIMT_MAX")) simt_max = atoi(e);
-    p.simt_attention = p.seq <= simt_max;
-  }
   p.gather[0] = !exact && p.seq > kSampleThreshold;
   p.gather[1] = !exact && p.mseq > kSampleThreshold;
   p.rows_c = (p.gather[0] || p.gather[1]) ? p.tmax0 / kSampleStride + cap_batch + 1 : kGemmTileM;

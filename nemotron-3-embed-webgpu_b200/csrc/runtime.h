@@ -90,7 +90,6 @@ struct DevicePlan {
   int device = 0;
   DeviceModel* dm = nullptr;
   int cap_batch = 0, seq = 0, mseq = 0;
-  bool simt_attention = false;  // CUDA-core attention kernel (short requests)
   int tmax0 = 0, tmax1 = 0;  // worst-case valid tokens before / after merge
   int rows0 = 0, rows1 = 0;  // tmax rounded up to the GEMM M tile
   cudaStream_t stream = nullptr;
