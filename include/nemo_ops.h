@@ -120,6 +120,14 @@ int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m
                             void* d_err, void* stream);
 int nemo_op_qmatmul(int fmt, const void* d_packed, const void* d_x, int m, int n, int k, void* d_y);
 
+/* Decode of a tile-slab image by the per-row decoders every projection kernel
+ * runs (the same launch model load uses to build the batched path's f16
+ * weights): d_w16 = f16(decode(blocks)) as a row-major [n x k] f16 matrix,
+ * 16-byte aligned. Replaces the reference's dequantisation for parity checks:
+ * src/gguf/quantization.ts:19-74 rounded to f16 as quant-matmul.ts:106 does.
+ * Synchronises. */
+int nemo_op_qmatmul_image_decode(int fmt, const void* d_image, int n, int k, void* d_w16);
+
 /* Routing of the head-parallel path (no reference counterpart; the index
  * functions its QKV GEMM and attention epilogues use, exported for layout
  * tests without a GPU), n_devices in {2, 4, 8}:

@@ -328,6 +328,14 @@ int nemo_op_qmatmul_image(int fmt, const void* d_packed, int n, int k, void* d_i
   return sync_and_check(launch_qmatmul_retile(fmt, (const uint8_t*)d_packed, n, k, (uint8_t*)d_image, 0));
 }
 
+int nemo_op_qmatmul_image_decode(int fmt, const void* d_image, int n, int k, void* d_w16) {
+  if (!d_image || !d_w16 || !qmatmul_image_bytes(fmt, n, k) || ((uintptr_t)d_image & 255) || ((uintptr_t)d_w16 & 15)) {
+    set_error("nemo_op_qmatmul_image_decode: bad arguments (n a multiple of 128, K divisible by 256, aligned buffers)");
+    return kErrArgs;
+  }
+  return sync_and_check(launch_qmatmul_image_decode(fmt, (const uint8_t*)d_image, n, k, (__half*)d_w16, 0));
+}
+
 int nemo_op_qmatmul_enqueue(int fmt, const void* d_image, const void* d_x, int m, int n, int k, void* d_y, void* d_err,
                             void* stream) {
   if (!d_image || !d_x || !d_y || !d_err || m < 1 || ((uintptr_t)d_image & 255) || ((uintptr_t)d_x & 15) ||

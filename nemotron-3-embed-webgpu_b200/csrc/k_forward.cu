@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const __grid_const
         }
         const uint8_t* region = raw + rs * CM + roff;
         const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
-        const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
+        const uint16_t d6 = fmt == kSegQ6K ? *reinterpret_cast<const uint16_t*>(region + 64 * 208 + rr * 2) : 0;
         const int s = it % kASlabs;
         if (!__all_sync(0xffffffffu, wait(aempty + 8 * s, ((it / kASlabs) & 1) ^ 1, err, lim))) {
           ok = false;

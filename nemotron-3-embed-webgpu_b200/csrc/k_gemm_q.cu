@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       if (!__all_sync(0xffffffffu, dev::mbar_wait(rfull + 8 * rs, (s / kQRaw) & 1, err))) break;
       const uint8_t* region = raw + rs * chunk_max + roff;
       const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
-      const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
+      const uint16_t d6 = fmt == kSegQ6K ? *reinterpret_cast<const uint16_t*>(region + 64 * 208 + rr * 2) : 0;
       bool ok = true;
 #pragma unroll 1
       for (int qq = 0; qq < 2; ++qq) {

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!dev::mbar_wait(rfull + 8 * rs, (i / RS) & 1, a.err)) break;
       const uint8_t* region = raw + rs * a.chunk_max + roff;
       const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
-      const float d6 = fmt == kSegQ6K ? half_at(region + 64 * 208 + rr * 2) : 0.f;
+      const uint16_t d6 = fmt == kSegQ6K ? *reinterpret_cast<const uint16_t*>(region + 64 * 208 + rr * 2) : 0;
       for (int q = 0; q < 4; ++q, ++sub) {
         const int s = sub % kAStages;
         if (!dev::mbar_wait(aempty + 8 * s, ((sub / kAStages) & 1) ^ 1, a.err)) {

@@ -273,6 +273,7 @@ cudaError_t launch_gemm_q(const CUtensorMap* map_x, const uint8_t* packed, const
 // m <= 64, dequant-fused GEMM above). err: device word for bounded waits.
 size_t qmatmul_image_bytes(int fmt, int n, int k);
 cudaError_t launch_qmatmul_retile(int fmt, const uint8_t* src, int n, int k, uint8_t* image, cudaStream_t s);
+cudaError_t launch_qmatmul_image_decode(int fmt, const uint8_t* image, int n, int k, __half* w16, cudaStream_t s);
 int qmatmul_enqueue(int fmt, const uint8_t* image, const __half* x, int m, int n, int k, float* y, uint32_t* err,
                     cudaStream_t s);
 

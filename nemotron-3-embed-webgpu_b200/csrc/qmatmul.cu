@@ -105,7 +105,7 @@ __global__ void decode_image_kernel(const uint8_t* __restrict__ chunks, const Sk
     const int mrow = interleave ? (half ? n / 2 + tile * 64 + rr : tile * 64 + rr) : tile * 128 + row;
     const GlobalRowSink sink{w16 + (size_t)mrow * k + slab * 256 + q * 64};
     if (fmt == kSegQ4K) decode_q4k(blk, q, sink);
-    else if (fmt == kSegQ6K) decode_q6k(blk, half_at(region + 64 * 208 + rr * 2), q, sink);
+    else if (fmt == kSegQ6K) decode_q6k(blk, *reinterpret_cast<const uint16_t*>(region + 64 * 208 + rr * 2), q, sink);
     else decode_q40(blk, q, sink);
   }
 }
@@ -131,6 +131,12 @@ cudaError_t launch_qmatmul_retile(int fmt, const uint8_t* src, int n, int k, uin
   const int total = n * (k / 256);
   retile_kernel<<<(total + 255) / 256, 256, 0, s>>>(fmt, src, n, k, image);
   return cudaGetLastError();
+}
+
+cudaError_t launch_qmatmul_image_decode(int fmt, const uint8_t* image, int n, int k, __half* w16, cudaStream_t s) {
+  if (!qmatmul_image_bytes(fmt, n, k)) return cudaErrorInvalidValue;
+  return launch_decode_image(image + q_table_bytes(n), reinterpret_cast<const SkinnyTile*>(image), n / 128, k / 256,
+                             false, n, k, w16, s);
 }
 
 int qmatmul_enqueue(int fmt, const uint8_t* image, const __half* x, int m, int n, int k, float* y, uint32_t* err,

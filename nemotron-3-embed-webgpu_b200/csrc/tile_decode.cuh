@@ -21,35 +21,6 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// --- packed f32x2 arithmetic (sm_100) ---------------------------------------
-__device__ __forceinline__ uint64_t f2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
-  float a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-  return pack_h2(a, b);
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-// 2^23 + n as f32 bits, for a small unsigned n.
-__device__ __forceinline__ float magic(uint32_t n) { return __uint_as_float(0x4B000000u | n); }
-
 __device__ __forceinline__ void st_chunk(uint8_t* a_tile, int r, int c, uint4 v) {
   *reinterpret_cast<uint4*>(a_tile + r * 128 + ((c ^ (r & 7)) << 4)) = v;
 }
@@ -74,16 +45,56 @@ struct RegSink {
 
 __device__ __forceinline__ int region_bytes(int fmt) { return fmt == kSegQ6K ? 64 * 210 : 64 * 144; }
 
-// Q4_K row block (GGUF 144 B). Quarter q = elements 64q..64q+63 of the slab.
-// value = f32(d*sc*q - dmin*m) (quantization.ts:33-34): s = d*sc and
-// o = dmin*m are exact; one rounding in the subtraction of o, as in the
-// reference. A nibble at bit p of a word is masked in place under the f32
-// exponent of 2^23: (w & (15 << p)) | 0x4B000000 = 2^23 + q * 2^p (p <= 12
-// here), and fma(s * 2^-p, 2^23 + q * 2^p, -s * 2^(23-p)) = s * q exactly
-// (s * 2^-p is exact: s >= 2^-24 stays far above the f32 subnormal range).
+// --- bit-level helpers -------------------------------------------------------
+// (a & b) | c in one logic op (the compiler otherwise splits a mask-and-or with
+// two constants into two).
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hadd2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// f32 result of f16 a times the low / high f16 half of b plus f32 c, rounded
+// once (the mixed-precision fma of sm_100: both f16 operands widen exactly).
+__device__ __forceinline__ float mixed_fma_lo(uint16_t a, uint32_t b, float c) {
+  float r;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %2; fma.rn.f32.f16 %0, %1, l, %3;}" : "=f"(r) : "h"(a), "r"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float mixed_fma_hi(uint16_t a, uint32_t b, float c) {
+  float r;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %2; fma.rn.f32.f16 %0, %1, h, %3;}" : "=f"(r) : "h"(a), "r"(b), "f"(c));
+  return r;
+}
+// f16 bits of v (exactly representable) in both halves.
+__device__ __forceinline__ uint32_t f16x2_bits(float v) {
+  const uint32_t b = __half_as_ushort(__float2half_rn(v));
+  return b | (b << 16);
+}
+
+// Q4_K row block (GGUF 144 B). Quarter q = elements 64q..64q+63 of the slab:
+// sub-block 2q in the low nibbles of quant bytes 32q..32q+31, sub-block 2q+1 in
+// their high nibbles. value = f32(d*sc*q - dmin*m) (quantization.ts:33-34):
+// d*sc*q is exact and the subtraction of dmin*m rounds once.
+// Here t = sc*q, an integer <= 945, is formed exactly in f16x2 arithmetic from
+// nibbles masked under the f16 exponent of 1024 ((w & 0x000F000F) | 0x64006400
+// = {1024 + q, 1024 + q'}; high nibbles give 1024 + 16q): t = fma(sc, 1024 + q,
+// -1024 sc), or fma(sc / 16, 1024 + 16 q, -64 sc). Then one mixed fma
+// d (f16) * t - dmin*m computes d*sc*q exactly and rounds the difference once:
+// the same f32 value, zero signs included.
 template <typename Sink>
 __device__ __forceinline__ void decode_q4k(const uint8_t* blk, int q, Sink&& sink) {
-  const float d = half_at(blk), dmin = half_at(blk + 2);
+  const uint16_t dh = *reinterpret_cast<const uint16_t*>(blk);
+  const float dmin = half_at(blk + 2);
   const uint8_t* s = blk + 4;
   const int lo = 2 * q, hi = 2 * q + 1;
   int sc_lo, m_lo, sc_hi, m_hi;
@@ -98,38 +109,41 @@ __device__ __forceinline__ void decode_q4k(const uint8_t* blk, int q, Sink&& sin
     sc_hi = (s[hi + 4] & 15) | ((s[hi - 4] >> 6) << 4);
     m_hi = (s[hi + 4] >> 4) | ((s[hi] >> 6) << 4);
   }
-  const float s_lo = __fmul_rn(d, (float)sc_lo), s_hi = __fmul_rn(d, (float)sc_hi);
-  const float o_lo = __fmul_rn(dmin, (float)m_lo), o_hi = __fmul_rn(dmin, (float)m_hi);
-  // low nibbles at bits 0 and 8, high nibbles at bits 4 and 12 (of w or w >> 16)
-  const uint64_t S_lo = f2(s_lo, __fmul_rn(s_lo, 0x1p-8f)), S_hi = f2(__fmul_rn(s_hi, 0x1p-4f), __fmul_rn(s_hi, 0x1p-12f));
-  const uint64_t C_lo = f2(-__fmul_rn(s_lo, 0x1p23f), -__fmul_rn(s_lo, 0x1p15f));
-  const uint64_t C_hi = f2(-__fmul_rn(s_hi, 0x1p19f), -__fmul_rn(s_hi, 0x1p11f));
-  const uint64_t O_lo = f2(-o_lo, -o_lo), O_hi = f2(-o_hi, -o_hi);
+  const float o_lo = -__fmul_rn(dmin, (float)m_lo), o_hi = -__fmul_rn(dmin, (float)m_hi);
+  const uint32_t SL = f16x2_bits((float)sc_lo), CL = f16x2_bits(-1024.f * sc_lo);
+  const uint32_t SH = f16x2_bits(0.0625f * sc_hi), CH = f16x2_bits(-64.f * sc_hi);
   const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + q * 32);
   const uint4 w0 = qv[0], w1 = qv[1];
   const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const uint32_t m0 = c < 4 ? 0x0Fu : 0xF0u, m1 = m0 << 8;
-    const uint64_t S = c < 4 ? S_lo : S_hi, C = c < 4 ? C_lo : C_hi, O = c < 4 ? O_lo : O_hi;
-    const uint32_t wa = w[(c & 3) * 2], wb = w[(c & 3) * 2 + 1];
-    uint32_t h[4];
+  for (int c = 0; c < 4; ++c) {  // words 2c, 2c+1: low chunk c and high chunk 4 + c
+    uint32_t lv[4], hv[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t src = i < 2 ? wa : wb;
-      const uint32_t x = (i & 1) ? src >> 16 : src;
-      const uint64_t qf = f2(__uint_as_float((x & m0) | 0x4B000000u), __uint_as_float((x & m1) | 0x4B000000u));
-      h[i] = f2_to_h2(fadd2(ffma2(S, qf, C), O));
+    for (int j = 0; j < 2; ++j) {  // word = bytes 4j..4j+3 of the chunk's 8
+      const uint32_t x = w[2 * c + j], y = x >> 8;
+      const uint32_t l02 = hfma2_bits(and_or(x, 0x000F000Fu, 0x64006400u), SL, CL);  // bytes 0, 2
+      const uint32_t l13 = hfma2_bits(and_or(y, 0x000F000Fu, 0x64006400u), SL, CL);  // bytes 1, 3
+      const uint32_t h02 = hfma2_bits(and_or(x, 0x00F000F0u, 0x64006400u), SH, CH);
+      const uint32_t h13 = hfma2_bits(and_or(y, 0x00F000F0u, 0x64006400u), SH, CH);
+      lv[2 * j] = pack_h2(mixed_fma_lo(dh, l02, o_lo), mixed_fma_lo(dh, l13, o_lo));
+      lv[2 * j + 1] = pack_h2(mixed_fma_hi(dh, l02, o_lo), mixed_fma_hi(dh, l13, o_lo));
+      hv[2 * j] = pack_h2(mixed_fma_lo(dh, h02, o_hi), mixed_fma_lo(dh, h13, o_hi));
+      hv[2 * j + 1] = pack_h2(mixed_fma_hi(dh, h02, o_hi), mixed_fma_hi(dh, h13, o_hi));
     }
-    sink(c, make_uint4(h[0], h[1], h[2], h[3]));
+    sink(c, make_uint4(lv[0], lv[1], lv[2], lv[3]));
+    sink(4 + c, make_uint4(hv[0], hv[1], hv[2], hv[3]));
   }
 }
 
-// Q6_K row block: ql[128] qh[64] scales[16] (208 B), d separate.
-// value = f32((d*sc) * (q - 32)) (quantization.ts:67-70): d*sc exact, q - 32
-// exact ((2^23+q) - (2^23+32)), one rounding in the product.
+// Q6_K row block: ql[128] qh[64] scales[16] (208 B); dh = the row's f16 d bits.
+// value = f32((d*sc) * (q - 32)) (quantization.ts:67-70): d*sc exact, one
+// rounding in the product. The 6-bit q of four consecutive elements are put
+// together in the bytes of one word (low 4 bits from ql, high 2 from qh); a
+// byte permute with 0x64 bytes makes f16 pairs 1024 + q, and adding -1056 gives
+// q - 32 exactly. d * (q - 32) is exact in f32 (mixed fma with a -0 addend,
+// which keeps the sign of a zero product), and the product with sc rounds once.
 template <typename Sink>
-__device__ __forceinline__ void decode_q6k(const uint8_t* blk, float d, int q, Sink&& sink) {
+__device__ __forceinline__ void decode_q6k(const uint8_t* blk, uint16_t dh, int q, Sink&& sink) {
   const int h = q >> 1, odd = q & 1;
   const uint8_t* ql = blk + h * 64;
   const uint8_t* qh = blk + 128 + h * 32;
@@ -139,25 +153,24 @@ __device__ __forceinline__ void decode_q6k(const uint8_t* blk, float d, int q, S
   const uint4 h0 = reinterpret_cast<const uint4*>(qh)[0], h1 = reinterpret_cast<const uint4*>(qh)[1];
   const uint32_t lw[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w, l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
   const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-  const int nsh = odd ? 4 : 0;
-  const uint64_t M32 = f2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+  const uint32_t kM1056 = 0xE420E420u;  // f16 -1056 in both halves
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int qi = c >> 2;
     const int lane0 = (c & 3) * 8;
-    const int hsh = 4 * odd + 2 * qi;
-    const float ds = __fmul_rn(d, (float)sc[(2 * odd + qi) * 2 + lane0 / 16]);
-    const uint64_t DS = f2(ds, ds);
-    const uint32_t la = lw[qi * 8 + lane0 / 4], lb = lw[qi * 8 + lane0 / 4 + 1];
-    const uint32_t ha = hw[lane0 / 4], hb = hw[lane0 / 4 + 1];
+    const int hsh = 4 * odd + 2 * qi;  // bit of the element's 2 high bits in its qh byte
+    const float s = (float)sc[(2 * odd + qi) * 2 + lane0 / 16];
     uint32_t hv[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t L = i < 2 ? la : lb, H = i < 2 ? ha : hb;
-      const int b0 = (i & 1) * 2;
-      const uint32_t qa = ((L >> (8 * b0 + nsh)) & 15u) | (((H >> (8 * b0 + hsh)) & 3u) << 4);
-      const uint32_t qb = ((L >> (8 * b0 + 8 + nsh)) & 15u) | (((H >> (8 * b0 + 8 + hsh)) & 3u) << 4);
-      hv[i] = f2_to_h2(fmul2(DS, fadd2(f2(magic(qa), magic(qb)), M32)));
+    for (int j = 0; j < 2; ++j) {  // elements 4j..4j+3 of the chunk
+      const uint32_t L = odd ? lw[qi * 8 + lane0 / 4 + j] >> 4 : lw[qi * 8 + lane0 / 4 + j];
+      const uint32_t Hs = hw[lane0 / 4 + j];
+      const uint32_t H = hsh >= 4 ? Hs >> (hsh - 4) : Hs << (4 - hsh);
+      const uint32_t qb = and_or(L, 0x0F0F0F0Fu, H & 0x30303030u);
+      const uint32_t t01 = hadd2_bits(__byte_perm(qb, 0x64646464u, 0x5140u), kM1056);
+      const uint32_t t23 = hadd2_bits(__byte_perm(qb, 0x64646464u, 0x5342u), kM1056);
+      hv[2 * j] = pack_h2(__fmul_rn(mixed_fma_lo(dh, t01, -0.f), s), __fmul_rn(mixed_fma_hi(dh, t01, -0.f), s));
+      hv[2 * j + 1] = pack_h2(__fmul_rn(mixed_fma_lo(dh, t23, -0.f), s), __fmul_rn(mixed_fma_hi(dh, t23, -0.f), s));
     }
     sink(c, make_uint4(hv[0], hv[1], hv[2], hv[3]));
   }
@@ -190,10 +203,10 @@ __device__ __forceinline__ void decode_q40(const uint8_t* blk, int q, Sink&& sin
         const uint32_t pair = __byte_perm(src, 0, (i & 1) ? 0x4342u : 0x4140u);  // bytes -> low bytes of halves
         __half2 qh;
         if (!high) {
-          const uint32_t m = (pair & 0x000F000Fu) | 0x64006400u;  // 1024 + q
+          const uint32_t m = and_or(pair, 0x000F000Fu, 0x64006400u);  // 1024 + q
           qh = __hsub2(*reinterpret_cast<const __half2*>(&m), k1032);
         } else {
-          const uint32_t m = (pair & 0x00F000F0u) | 0x64006400u;  // 1024 + 16q
+          const uint32_t m = and_or(pair, 0x00F000F0u, 0x64006400u);  // 1024 + 16q
           qh = __hfma2(*reinterpret_cast<const __half2*>(&m), k16th, k72);
         }
         const __half2 v = __hmul2(d2, qh);

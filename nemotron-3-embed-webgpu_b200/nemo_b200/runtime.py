@@ -88,6 +88,7 @@ def load_library() -> ctypes.CDLL:
         "nemo_op_qmatmul_image_bytes": (S, [I, I, I]),
         "nemo_op_qmatmul_image": (I, [I, P, I, I, P]),
         "nemo_op_qmatmul_enqueue": (I, [I, P, P, I, I, I, P, P, P]),
+        "nemo_op_qmatmul_image_decode": (I, [I, P, I, I, P]),
         "nemo_op_qmatmul": (I, [I, P, P, I, I, I, P]),
         "nemo_hp_qkv_route": (I, [I, P, P, P]),
         "nemo_hp_row_owner": (I, [I, I, I, P]),

@@ -127,6 +127,45 @@ def test_qmatmul_enqueue_on_image_repeats_bit_identically(rng):
         assert rel_err(outs[0], ref32) < TOL
 
 
+def signed_blocks(rng, fmt, rows, k):
+    """blocks() with the sign of d (and of dmin for Q4_K) flipped on random
+    blocks and the scales of a quarter of the blocks zeroed, so that zero
+    products of either sign occur."""
+    w, code, compact = blocks(rng, fmt, rows, k)
+    b = w.reshape(-1, 144 if fmt == 0 else 210).copy()
+    flip = rng.random(len(b)) < 0.5
+    zero = rng.random(len(b)) < 0.25
+    if fmt == 0:
+        b[flip, 1] |= 0x80
+        b[rng.random(len(b)) < 0.5, 3] |= 0x80
+        b[zero, 4:16] = 0
+        b[rng.random(len(b)) < 0.25, 8:12] = 0  # mins of sub-blocks 0-3
+    else:
+        b[flip, 209] |= 0x80
+        b[zero, 192:208] = 0
+    return b.reshape(-1), code, compact
+
+
+@pytest.mark.parametrize("case", ["q4_k", "q6_k", "q4_0", "q4_0_tile32", "q4_k_signed", "q6_k_signed"])
+def test_tile_slab_decoders_bit_exact(rng, case):
+    """The per-row decoders every projection kernel runs on the tile-slab
+    image (single-launch forward, split-K small-token kernel, dequant-fused
+    GEMM, and model load's f16 weights) give f16(decode(blocks)) bit for bit,
+    zero signs included (quantization.ts:19-74, f16 rounding as
+    quant-matmul.ts:106)."""
+    t = __import__("torch")
+    fmt = FMT_IDS.index(case.replace("_signed", ""))
+    n, k = 384, 2048
+    w, code, compact = (signed_blocks if case.endswith("signed") else blocks)(rng, fmt, n, k)
+    d_w = dev(w)
+    image = t.zeros(L().nemo_op_qmatmul_image_bytes(fmt, n, k), dtype=t.uint8, device="cuda")
+    check(L().nemo_op_qmatmul_image(fmt, ptr(d_w), n, k, ptr(image)))
+    w16 = t.full((n, k), float("nan"), dtype=t.float16, device="cuda")
+    check(L().nemo_op_qmatmul_image_decode(fmt, ptr(image), n, k, ptr(w16)))
+    want = oracle.decode_matrix(w, code, compact, k, n).astype(np.float16)
+    assert np.array_equal(host(w16).view(np.uint16), want.view(np.uint16))
+
+
 def test_qmatmul_rejects_bad_shapes(rng):
     t = __import__("torch")
     w = dev(np.zeros(256 * 144, np.uint8))
