@@ -12,11 +12,14 @@
 //               before waiting on the previous kernel, then TMA-loads the
 //               activation K range (box 64 x NP, 128B swizzle)
 //   warp 1      TMEM allocation + tcgen05.mma issue (elected lane)
-//   warps 2..5  decoders (thread = weight row): exact decode of the block
+//   warps 2..9  decoders (thread = weight row): exact decode of the block
 //               with the reference's arithmetic (quantization.ts:19-74; every
 //               intermediate is exact or rounded once, as there), f16 round to
-//               nearest, written in the canonical 128B-swizzled K-major layout;
-//               then TMEM -> this CTA's partial tile in shared memory.
+//               nearest, written in the canonical 128B-swizzled K-major layout.
+//               Warps 2-5 decode the even 64-column quarters of each slab into
+//               A stage 0, warps 6-9 the odd ones into stage 1, so two quarters
+//               are decoded at once; warps 2-5 then move TMEM -> this CTA's
+//               partial tile in shared memory.
 // The split-K CTAs of one tile are one thread-block cluster: after a cluster
 // barrier each CTA reduces a slice of the tile's rows from its peers' shared
 // memory (DSMEM), summing the splits in rank order (deterministic), and applies
@@ -33,11 +36,12 @@ constexpr int kMaxRawStages = 3;
 constexpr int kAStages = 2;
 constexpr int kABytes = 128 * 128;  // 128 rows x 64 f16
 constexpr int kMaxSplits = 16;
+constexpr int kThreads = 320;  // producer, MMA issuer, two groups of four decoder warps
 
 using namespace tsd;
 
 template <int NP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     skinny_kernel(const __grid_constant__ CUtensorMap map_x, SkinnyArgs a) {
   extern __shared__ uint8_t smem_raw[];
   dev::pdl_launch_dependents();
@@ -67,7 +71,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::mbar_init(xfull, 1);
     for (int s = 0; s < kMaxRawStages; ++s) {
       dev::mbar_init(rfull + 8 * s, 1);
-      dev::mbar_init(rempty + 8 * s, 128);
+      dev::mbar_init(rempty + 8 * s, 256);
     }
     for (int s = 0; s < kAStages; ++s) {
       dev::mbar_init(afull + 8 * s, 128);
@@ -154,8 +158,9 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
     dev::mbar_wait(accum, 0, a.err, 100000000ull);
   } else {
-    // ---- decoders: thread = weight row of the tile ----
-    const int r = threadIdx.x - 64;
+    // ---- decoders: thread = weight row of the tile; group grp decodes the
+    // quarters q = grp, grp + 2 of every slab into A stage grp ----
+    const int r = (threadIdx.x - 64) & 127, grp = (threadIdx.x - 64) >> 7;
     const int half = r >> 6, rr = r & 63;
     const int fmt = ti.fmt[half];
     const int roff = half ? region_bytes(ti.fmt[0]) : 0;
@@ -167,7 +172,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint8_t* region = raw + rs * a.chunk_max + roff;
       const uint8_t* blk = region + rr * (fmt == kSegQ6K ? 208 : 144);
       const uint16_t d6 = fmt == kSegQ6K ? *reinterpret_cast<const uint16_t*>(region + 64 * 208 + rr * 2) : 0;
-      for (int q = 0; q < 4; ++q, ++sub) {
+      for (int q = grp; q < 4; q += kAStages) {
+        sub = i * 4 + q;  // A stage sub % kAStages = grp
         const int s = sub % kAStages;
         if (!dev::mbar_wait(aempty + 8 * s, ((sub / kAStages) & 1) ^ 1, a.err)) {
           ok = false;
@@ -184,11 +190,11 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_arrive(rempty + 8 * rs);
     }
     // ---- TMEM -> this CTA's partial tile in shared memory (red[t][row], f32;
-    // the raw ring is free once every chunk has been decoded) ----
+    // the raw ring is free once every chunk has been decoded), by warps 2-5 ----
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     float* red = reinterpret_cast<float*>(raw);
-    if (__all_sync(0xffffffffu, dev::mbar_wait(accum, 0, a.err))) {  // warp-uniform: tcgen05.ld is collective
+    if (grp == 0 && __all_sync(0xffffffffu, dev::mbar_wait(accum, 0, a.err))) {  // warp-uniform: tcgen05.ld is collective
       dev::tc_fence_after();
 #pragma unroll
       for (int c0 = 0; c0 < NP; c0 += 16) {
@@ -296,7 +302,7 @@ cudaError_t launch_skinny(const CUtensorMap* map_x, const SkinnyArgs& a, int np,
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, a.splits);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
