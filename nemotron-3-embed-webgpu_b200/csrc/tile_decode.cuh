@@ -1,10 +1,11 @@
 // Tile-slab weight decoders shared by the fused-dequant projection kernels
-// (k_skinny.cu, k_forward.cu). A decoder thread owns one weight row of a
-// 128-row tile and turns one 64-value quarter of a 256-column slab into eight
-// 16-byte chunks of the canonical 128B-swizzled K-major f16 A tile that
-// tcgen05.mma reads. Values follow the reference's decode arithmetic exactly
-// (quantization.ts:19-74); each intermediate is exact or rounded once, as
-// there, and the f16 store rounds to nearest even.
+// (k_forward.cu, k_skinny.cu, k_gemm_q.cu) and by the image decode of model
+// load and nemo_op_qmatmul_image_decode (qmatmul.cu). A decoder thread owns
+// one weight row of a 128-row tile and turns one 64-value quarter of a
+// 256-column slab into eight 16-byte chunks of the canonical 128B-swizzled
+// K-major f16 A tile that tcgen05.mma reads. Values follow the reference's
+// decode arithmetic exactly (quantization.ts:19-74); each intermediate is
+// exact or rounded once, as there, and the f16 store rounds to nearest even.
 #pragma once
 
 #include "kernels.cuh"
