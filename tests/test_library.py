@@ -41,3 +41,9 @@ def test_host_only_entry_points():
     assert lib.nemo_op_qmatmul_image_bytes(0, 2048, 2048) == 256 + 16 * 8 * 18432
     assert lib.nemo_op_qmatmul_image_bytes(1, 256, 6144) == 256 + 2 * 24 * 26880
     assert lib.nemo_op_qmatmul_image_bytes(0, 200, 2048) == 0
+    # the image decode rejects bad arguments before touching a device
+    assert lib.nemo_op_qmatmul_image_decode(0, None, 256, 2048, None) == -1
+    assert b"nemo_op_qmatmul_image_decode" in lib.nemo_last_error()
+    fake = ctypes.c_void_p(256)
+    assert lib.nemo_op_qmatmul_image_decode(0, fake, 200, 2048, fake) == -1
+    assert lib.nemo_op_qmatmul_image_decode(0, fake, 256, 2000, fake) == -1
